@@ -1,0 +1,470 @@
+#!/usr/bin/env python
+"""Benchmark of the GQA decode-attention hot path (config 5 for N > 1).
+
+One step = one Qwen3-4B decode token's attention over all 36 layers: q [1, 32, 128] per layer
+against that layer's static KV of L = 8192 keys per GPU, laid out [layer, 2, nkv=8, max_len,
+hd=128] bf16 in HBM (1.2 GB per GPU, larger than the 126 MB L2, so consecutive layers never hit in
+L2). Inputs are seeded synthetic tensors with the reference's pipeline: N(0,1) -> QK-RMSNorm
+(eps 1e-6) -> RoPE (theta 1e6). The 36 calls are captured in one CUDA graph and replayed.
+
+N > 1 (torchrun): the sequence is sharded, context 8192 * N with 8192 keys per rank (weak
+scaling); per layer each rank computes a partial (O, LSE) of its shard, the partials are
+all-gathered with NCCL over NVLink and merged with the LSE-merge kernel on every rank.
+
+Prints ONE JSON line (rank 0). ``value`` = KV bytes read by all ranks per second (GB/s).
+``--impl reference`` times the reference's CPU attention path (the grouped decode of
+``cuda_graph_executor.py:180-184``, restated in ``oracle/``) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LAYERS, NH, NKV, HD = 36, 32, 8, 128
+THETA, EPS = 1e6, 1e-6
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ctx", type=int, default=8192, help="keys per GPU")
+    ap.add_argument("--cpu-sample-s", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true", help="also time L in {128..8192} (stderr)")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        import tempfile
+
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as fh:
+            for line in fh:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].isdigit():
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows
+                                                         if r[3].replace(".", "").isdigit())}
+
+
+# ------------------------------------------------------------------------------------------
+# synthetic inputs (on the device)
+# ------------------------------------------------------------------------------------------
+def _rmsnorm(x, eps=EPS):
+    d = x.float()
+    return (d * (d.pow(2).mean(-1, keepdim=True) + eps).rsqrt()).to(x.dtype)
+
+
+def _rope(x, pos, dtype):
+    import torch
+
+    inv = 1.0 / (THETA ** (torch.arange(0, HD, 2, device=x.device).float() / HD))
+    f = pos[:, None].float() * inv[None, :]
+    emb = torch.cat([f, f], -1)
+    cos, sin = emb.cos().to(dtype), emb.sin().to(dtype)
+    while cos.dim() < x.dim():
+        cos, sin = cos.unsqueeze(-2), sin.unsqueeze(-2)
+    h = HD // 2
+    return x * cos + torch.cat([-x[..., h:], x[..., :h]], -1) * sin
+
+
+def make_inputs(ctx: int, rank: int, world: int, device, seed: int = 2024):
+    """KV [36, 2, 8, ctx, 128] for keys [rank*ctx, (rank+1)*ctx) of a ctx*world context, and the
+    36 layers' query [36, 1, 1, 32, 128] at position ctx*world - 1 (same on every rank)."""
+    import torch
+
+    bf = torch.bfloat16
+    kv = torch.empty(LAYERS, 2, NKV, ctx, HD, dtype=bf, device=device)
+    pos = torch.arange(rank * ctx, (rank + 1) * ctx, device=device)
+    g = torch.Generator(device=device)
+    for li in range(LAYERS):
+        g.manual_seed(seed * 1000 + li * 16 + rank)
+        k = torch.randn(ctx, NKV, HD, generator=g, device=device).to(bf)
+        v = torch.randn(ctx, NKV, HD, generator=g, device=device).to(bf)
+        kv[li, 0] = _rope(_rmsnorm(k), pos, bf).transpose(0, 1)
+        kv[li, 1] = v.transpose(0, 1)
+    g.manual_seed(seed)
+    q = torch.randn(LAYERS, 1, 1, NH, HD, generator=g, device=device).to(bf)
+    qpos = torch.full((1,), ctx * world - 1, dtype=torch.int64, device=device)
+    q = _rope(_rmsnorm(q), qpos.repeat(1), bf)
+    return kv, q, qpos
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline / reference arm: the reference's grouped decode on the host cores
+# ------------------------------------------------------------------------------------------
+def cpu_reference_rate(ctx: int, budget_s: float, threads: int) -> dict:
+    import torch
+
+    from oracle import attention as A
+
+    torch.set_num_threads(threads)
+    q, k, v = A.make_attention_inputs(7, NH, NKV, HD, 1, ctx, ctx - 1)
+    scale = HD ** -0.5
+    A.decode_reference_grouped(q[0], k, v, ctx - 1, ctx, scale)  # warm
+    n, t0 = 0, time.perf_counter()
+    while True:
+        A.decode_reference_grouped(q[0], k, v, ctx - 1, ctx, scale)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s or n >= 100000:
+            break
+    per_call = el / n
+    gbs = 2 * ctx * NKV * HD * 2 / per_call / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} single-layer calls of the reference grouped decode "
+                      f"(cuda_graph_executor.py:180-184, restated in oracle/) at L={ctx}, "
+                      f"32/8 heads, bf16 on CPU; {per_call * 1e3:.2f} ms/call",
+            "ms_per_layer_call": round(per_call * 1e3, 4)}
+
+
+def run_reference_arm(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    threads = os.cpu_count() or 1
+    per_step_budget = max(1.0, args.cpu_sample_s / max(1, args.steps))
+    # warmup
+    for _ in range(args.warmup):
+        cpu_reference_rate(args.ctx, 0.2, threads)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        vals.append(cpu_reference_rate(args.ctx, per_step_budget, threads))
+    wall = time.perf_counter() - t0
+    value = statistics.median(v["value"] for v in vals)
+    ms_layer = statistics.median(v["ms_per_layer_call"] for v in vals)
+    line = {
+        "impl": "reference",
+        "metric": "GQA decode-attn HBM GB/s",
+        "value": value, "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_layer * LAYERS, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) -> QK-RMSNorm -> RoPE theta 1e6)",
+        "config": {"workload": f"qwen3-4b decode attention, L={args.ctx}, 32/8 heads, hd 128",
+                   "sample": "per step: single-layer calls for a bounded time, x36 layers"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": vals[0]["sample"]},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": round(wall, 2),
+        "torch_threads": torch.get_num_threads(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------
+def run_gpu_arm(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from solort_b200 import ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    ctx = args.ctx
+    kv, q, qpos = make_inputs(ctx, rank, world, dev)
+    bytes_per_layer = 2 * ctx * NKV * HD * 2  # K + V of this rank's keys
+    outs = torch.empty_like(q)
+    ws = torch.empty(max(256, ops.decode_workspace_bytes(1, 1, NH, NKV, ctx)), dtype=torch.uint8,
+                     device=dev)
+    sharded = None
+    if world > 1:
+        from solort_b200.sharded import ShardedDecode
+
+        sharded = ShardedDecode(rank, world, num_qo_heads=NH, layers=LAYERS, device=dev)
+
+    def step():
+        for li in range(LAYERS):
+            if sharded is None:
+                ops.gqa_decode(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND",
+                               out=outs[li], workspace=ws)
+            else:
+                sharded.layer(li, q[li], kv[li, 0], kv[li, 1], qpos, rank * ctx, outs[li], ws)
+
+    # capture one step in a graph (side-stream warm-up first, as the reference does)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    torch.cuda.synchronize(dev)
+
+    # correctness spot check of layer 0 against a torch fp32 evaluation on the device
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    if world == 1:
+        _spot_check(q[0], kv[0], outs[0], ctx)
+
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    if rank == 0:
+        clocks.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end) / args.steps
+    clk = clocks.stop() if rank == 0 else None
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    # e2e through the public API with host buffers: per step, pinned q -> device, the 36 layer
+    # calls (eager ctypes calls on the current stream), output -> pinned host.
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty_like(q_host).pin_memory()
+    calls = []
+    if sharded is None:
+        calls = [ops.DecodeCall(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND",
+                                out=outs[li], workspace=ws) for li in range(LAYERS)]
+
+    def e2e_step():
+        q.copy_(q_host, non_blocking=True)
+        if sharded is None:
+            for c in calls:
+                c()
+        else:
+            step()
+        out_host.copy_(outs, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(5, args.steps // 2)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    sweep = None
+    if args.sweep and world == 1:
+        sweep = _sweep(kv, q, qpos, ws, dev)
+
+    total_bytes = bytes_per_layer * LAYERS * world
+    value = total_bytes / (ms / 1e3) / 1e9
+    e2e_value = total_bytes / (e2e_ms / 1e3) / 1e9
+    per_call_us = ms * 1e3 / LAYERS
+    peaks = _peaks()
+    achieved = bytes_per_layer / (per_call_us * 1e-6) / 1e9
+    line = {
+        "metric": "GQA decode-attn HBM GB/s",
+        "value": round(value, 1),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) -> QK-RMSNorm eps 1e-6 -> RoPE theta 1e6)",
+        "config": {
+            "workload": "qwen3-4b static-KV single-token decode attention (BASELINE config 2"
+                        + (", seq-sharded per config 5)" if world > 1 else ")"),
+            "layers": LAYERS, "num_qo_heads": NH, "num_kv_heads": NKV, "head_dim": HD,
+            "keys_per_gpu": ctx, "context": ctx * world,
+            "kv_layout": "[layer, 2, nkv, max_len, hd] bf16",
+            "parallelism": f"seq-shard x{world}" if world > 1 else "single GPU",
+            "l2": "inputs larger than L2: 36 layers x 32 MiB KV per GPU replayed in order",
+            "graph": "36 layer calls per CUDA graph replay",
+        },
+        "pct_of_8TBs": round(100 * value / world / 8000, 2),
+        "roofline": {
+            "bound": "hbm",
+            "kernel": "one attention call = decode_kernel (split-KV) + lse_merge_kernel",
+            "achieved": round(achieved, 1),
+            "peak": peaks[0],
+            "unit": "GB/s",
+            "frac": round(achieved / peaks[0], 4),
+            "peak_source": peaks[1],
+            "algorithmic_bytes_per_launch": bytes_per_layer,
+            "us_per_launch": round(per_call_us, 3),
+            "traffic": None,
+        },
+        "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
+                "h2d_bytes_per_step": q_host.numel() * 2,
+                "d2h_bytes_per_step": out_host.numel() * 2,
+                "ms_per_step": round(e2e_ms, 4),
+                "how": "ops.DecodeCall per layer from Python, pinned H2D of the 36 queries and "
+                       "D2H of the 36 outputs inside the timed region"},
+        "gpu_launches": LAYERS * (2 if world == 1 else 3) * args.steps,
+        "clocks": clk,
+    }
+    if sweep:
+        line["sweep"] = sweep
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference_rate(ctx, args.cpu_sample_s, os.cpu_count() or 1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del graph
+    if sharded is not None:
+        sharded.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _spot_check(q, kv, out, ctx):
+    import torch
+
+    qf = q[0, 0].float().view(NKV, NH // NKV, HD)
+    k = kv[0].float()
+    v = kv[1].float()
+    s = torch.matmul(qf, k.transpose(1, 2)) * HD ** -0.5
+    ref = torch.matmul(torch.softmax(s, -1), v).reshape(NH, HD)
+    d = (out[0, 0].float() - ref).abs()
+    if d.max().item() > 2e-2 or d.mean().item() > 2e-3:
+        raise SystemExit(f"spot check failed: max {d.max().item()} mean {d.mean().item()}")
+
+
+def _sweep(kv, q, qpos_full, ws, dev):
+    import torch
+
+    from solort_b200 import ops
+
+    res = {}
+    for L in (128, 512, 1024, 2048, 4096, 8192):
+        qpos = torch.full((1,), L - 1, dtype=torch.int64, device=dev)
+        out = torch.empty_like(q)
+
+        def step():
+            for li in range(LAYERS):
+                ops.gqa_decode(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND", out=out[li],
+                               workspace=ws, max_kv_len=L)
+
+        step()
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        for _ in range(3):
+            g.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        n = 20
+        for _ in range(n):
+            g.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        ms = a.elapsed_time(b) / n
+        byt = 2 * L * NKV * HD * 2
+        res[str(L)] = {"us_per_layer": round(ms * 1e3 / LAYERS, 3),
+                       "GBs": round(byt * LAYERS / (ms / 1e3) / 1e9, 1),
+                       "l2_resident": L * 4096 * LAYERS <= 100 * 2**20}
+        del g
+    return res
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s"
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_gpu_arm(args)
+
+
+if __name__ == "__main__":
+    main()

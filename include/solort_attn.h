@@ -1,0 +1,150 @@
+/*
+ * solort_attn.h -- C ABI of the B200 (sm_100a) grouped-query attention engine for SoloRT's Qwen3
+ * fast path.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes; no torch types cross
+ * this boundary. All kernels are enqueued on the caller's stream (a cudaStream_t passed as
+ * `void*`), never allocate, never synchronise the host, and read lengths / positions from device
+ * memory, so every call can be captured inside a CUDA graph. Return value: SOLORT_OK (0) or a
+ * negative SOLORT_ERR_* code; no exception crosses the ABI and nothing falls back to another
+ * implementation.
+ *
+ * The reference (owen920831/SoloRT) computes this attention inline in torch; the entry points
+ * replace these call sites (paths inside the reference project):
+ *   solort_attn_decode, q_len == 1, static KV:
+ *       src/solort/model/cuda_graph_executor.py:168,180-184   (grouped decode + live-length mask)
+ *   solort_attn_decode, q_len == K+1, static KV:
+ *       src/solort/model/cuda_graph_executor.py:250,261-263   (verify: masked SDPA over max_len)
+ *   solort_attn_decode with a block table (paged KV, NHD pages [pages, 2, P, nkv, hd]):
+ *       src/solort/backends/transformers_flashinfer.py:95-129  (AttentionInterface decode/prefill)
+ *       src/solort/cache/kv_cache.py:86-100,136-149            (page layout, slot = bt[p//P]*P+p%P)
+ *   solort_attn_decode with out_f32/lse_out + solort_attn_lse_merge:
+ *       no counterpart (the reference is single-GPU); sequence-sharded long-context decode.
+ */
+#ifndef SOLORT_ATTN_H_
+#define SOLORT_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SOLORT_ATTN_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define SOLORT_API __attribute__((visibility("default")))
+#else
+#define SOLORT_API
+#endif
+
+/* Status codes. */
+#define SOLORT_OK 0
+#define SOLORT_ERR_INVALID_ARGUMENT (-1) /* null pointer, bad size, misaligned pointer/stride */
+#define SOLORT_ERR_UNSUPPORTED (-2)      /* head_dim != 128, too many query rows per KV head */
+#define SOLORT_ERR_WORKSPACE (-3)        /* workspace missing or smaller than required */
+#define SOLORT_ERR_CUDA (-4)             /* a CUDA runtime call or kernel launch failed */
+#define SOLORT_ERR_TENSOR_MAP (-5)       /* the driver rejected a TMA descriptor */
+#define SOLORT_ERR_NO_DEVICE (-6)        /* no sm_100 device is current */
+
+/*
+ * GQA attention of q_len query tokens per sequence against a KV cache: decode (q_len == 1),
+ * speculative verify / chunked append (q_len > 1), static buffer or paged.
+ *
+ * Shapes (element strides; head_dim must be 128 and contiguous):
+ *   q    [batch, q_len, num_qo_heads, head_dim] bf16
+ *   out  [batch, q_len, num_qo_heads, head_dim] bf16
+ *   K, V static  : element (token t, kv head h, dim d) at k + t*kv_stride_token
+ *                  + h*kv_stride_head + d  (NHD [max_len, nkv, hd] or HND [nkv, max_len, hd])
+ *   K, V paged   : element (page p, row r, head h, dim d) at k + p*kv_stride_page
+ *                  + r*kv_stride_token + h*kv_stride_head + d; V likewise from v. For SoloRT's
+ *                  NHD arena [pages, 2, P, nkv, hd]: v = k + P*nkv*hd, kv_stride_page = 2*P*nkv*hd.
+ *   block_table  [batch, >= ceil(kv_len/P)] int32 physical page ids (NULL for a static cache)
+ *
+ * Positions (read on the device, so the call can sit in a graph whose position changes):
+ *   q_pos[b] (int64) is the absolute position of query row 0 of sequence b; query row i sits at
+ *   q_pos[b] + i and attends key position j iff j <= q_pos[b] + i. Local key t of this cache sits
+ *   at position kv_pos_offset + t (0 unless the cache is one shard of a longer sequence).
+ *   q_lens (int32 [batch], optional) gives a per-sequence query count <= q_len; rows past it are
+ *   neither computed nor written.
+ *   max_kv_len is a host-side upper bound on the number of local keys any row sees; it sizes the
+ *   grid (the reference's decode bucket `bound`). Keys past it are not read.
+ *
+ * Outputs: by default bf16 `out`. If lse_out != NULL the call instead writes the normalised fp32
+ * output to out_f32 [batch, q_len, num_qo_heads, head_dim] (contiguous) and the natural-log
+ * log-sum-exp of the scaled scores to lse_out [batch, q_len, num_qo_heads]; rows that see no key
+ * get out_f32 = 0, lse = -inf. These partials combine with solort_attn_lse_merge.
+ *
+ * Workspace: split-KV partials; query solort_attn_decode_workspace_size() with the same args.
+ */
+typedef struct SolortDecodeArgs {
+  const void* q;
+  int64_t q_stride_batch, q_stride_token, q_stride_head;
+  void* out;
+  int64_t out_stride_batch, out_stride_token, out_stride_head;
+  float* out_f32;
+  float* lse_out;
+
+  const void* k;
+  const void* v;
+  int64_t kv_stride_token, kv_stride_head, kv_stride_page;
+  int32_t kv_capacity; /* static: tokens in the buffer. paged: ignored */
+
+  const int32_t* block_table;
+  int64_t block_table_stride;
+  int32_t page_size; /* power of two >= 8 */
+  int32_t num_pages; /* physical pages in the arena */
+
+  const int64_t* q_pos;
+  const int32_t* q_lens;
+  int64_t kv_pos_offset;
+
+  int32_t batch, q_len, num_qo_heads, num_kv_heads, head_dim;
+  int32_t max_kv_len;
+  float scale;
+  int32_t num_splits; /* 0 = choose for the device; otherwise the number of key splits */
+
+  void* workspace;
+  size_t workspace_bytes;
+} SolortDecodeArgs;
+
+SOLORT_API int solort_attn_decode_workspace_size(const SolortDecodeArgs* args, size_t* bytes);
+SOLORT_API int solort_attn_decode(const SolortDecodeArgs* args, void* stream);
+
+/*
+ * Merge num_parts partial results over disjoint key sets into one:
+ *   O = sum_p exp(lse_p - lse*) O_p / sum_p exp(lse_p - lse*),  lse = lse* + log(sum_p ...).
+ * o_parts: part p, row r at o_parts + p*part_stride + r*head_dim (fp32, head_dim contiguous);
+ * lse_parts: part p, row r at lse_parts + p*lse_part_stride + r.
+ * Rows are (batch, token, head) flattened, rows = batch*q_len*num_qo_heads. Writes bf16 `out`
+ * (strided like SolortDecodeArgs.out) unless out_f32 != NULL, in which case it writes fp32
+ * out_f32[r*head_dim + d] and lse_out[r].
+ */
+typedef struct SolortMergeArgs {
+  const float* o_parts;
+  int64_t part_stride;
+  const float* lse_parts;
+  int64_t lse_part_stride;
+  int32_t num_parts;
+  int32_t batch, q_len, num_qo_heads, head_dim;
+  void* out;
+  int64_t out_stride_batch, out_stride_token, out_stride_head;
+  float* out_f32;
+  float* lse_out;
+} SolortMergeArgs;
+
+SOLORT_API int solort_attn_lse_merge(const SolortMergeArgs* args, void* stream);
+
+/* Reads and clears the device status word of the current device (bit 0: an in-kernel wait hit
+ * its time limit and the kernel returned without writing its output). */
+SOLORT_API int solort_attn_device_status(unsigned* flags);
+
+SOLORT_API const char* solort_attn_status_string(int code);
+SOLORT_API int solort_attn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOLORT_ATTN_H_ */

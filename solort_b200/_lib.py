@@ -1,0 +1,153 @@
+"""ctypes binding of ``libsolort_attn.so`` (the C ABI declared in ``include/solort_attn.h``).
+
+The library is built in-tree by ``solort_b200.build``; it is loaded once, from the package
+directory. There is no fallback: if the library is missing or fails to load, importing the ops
+raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libsolort_attn.so")
+
+SOLORT_OK = 0
+STATUS_NAMES = {
+    0: "SOLORT_OK",
+    -1: "SOLORT_ERR_INVALID_ARGUMENT",
+    -2: "SOLORT_ERR_UNSUPPORTED",
+    -3: "SOLORT_ERR_WORKSPACE",
+    -4: "SOLORT_ERR_CUDA",
+    -5: "SOLORT_ERR_TENSOR_MAP",
+    -6: "SOLORT_ERR_NO_DEVICE",
+}
+
+# Every symbol the header declares; tests check the library exports each one.
+EXPORTED_SYMBOLS = (
+    "solort_attn_decode_workspace_size",
+    "solort_attn_decode",
+    "solort_attn_lse_merge",
+    "solort_attn_device_status",
+    "solort_attn_status_string",
+    "solort_attn_abi_version",
+)
+
+c_i32, c_i64, c_f32, c_vp, c_sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
+
+
+class SolortDecodeArgs(ctypes.Structure):
+    """Mirror of ``SolortDecodeArgs`` in ``include/solort_attn.h`` (same field order)."""
+
+    _fields_ = [
+        ("q", c_vp),
+        ("q_stride_batch", c_i64), ("q_stride_token", c_i64), ("q_stride_head", c_i64),
+        ("out", c_vp),
+        ("out_stride_batch", c_i64), ("out_stride_token", c_i64), ("out_stride_head", c_i64),
+        ("out_f32", c_vp),
+        ("lse_out", c_vp),
+        ("k", c_vp),
+        ("v", c_vp),
+        ("kv_stride_token", c_i64), ("kv_stride_head", c_i64), ("kv_stride_page", c_i64),
+        ("kv_capacity", c_i32),
+        ("block_table", c_vp),
+        ("block_table_stride", c_i64),
+        ("page_size", c_i32),
+        ("num_pages", c_i32),
+        ("q_pos", c_vp),
+        ("q_lens", c_vp),
+        ("kv_pos_offset", c_i64),
+        ("batch", c_i32), ("q_len", c_i32), ("num_qo_heads", c_i32), ("num_kv_heads", c_i32),
+        ("head_dim", c_i32),
+        ("max_kv_len", c_i32),
+        ("scale", c_f32),
+        ("num_splits", c_i32),
+        ("workspace", c_vp),
+        ("workspace_bytes", c_sz),
+    ]
+
+
+class SolortMergeArgs(ctypes.Structure):
+    """Mirror of ``SolortMergeArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("o_parts", c_vp),
+        ("part_stride", c_i64),
+        ("lse_parts", c_vp),
+        ("lse_part_stride", c_i64),
+        ("num_parts", c_i32),
+        ("batch", c_i32), ("q_len", c_i32), ("num_qo_heads", c_i32), ("head_dim", c_i32),
+        ("out", c_vp),
+        ("out_stride_batch", c_i64), ("out_stride_token", c_i64), ("out_stride_head", c_i64),
+        ("out_f32", c_vp),
+        ("lse_out", c_vp),
+    ]
+
+
+_LIB: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the in-tree library (once). Raises if it has not been built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m solort_b200.build` "
+            "(or __graft_entry__.build()); there is no non-CUDA fallback"
+        )
+    lib = ctypes.CDLL(LIB_PATH)
+    P = ctypes.POINTER
+    lib.solort_attn_decode_workspace_size.argtypes = [P(SolortDecodeArgs), P(c_sz)]
+    lib.solort_attn_decode_workspace_size.restype = ctypes.c_int
+    lib.solort_attn_decode.argtypes = [P(SolortDecodeArgs), c_vp]
+    lib.solort_attn_decode.restype = ctypes.c_int
+    lib.solort_attn_lse_merge.argtypes = [P(SolortMergeArgs), c_vp]
+    lib.solort_attn_lse_merge.restype = ctypes.c_int
+    lib.solort_attn_device_status.argtypes = [P(ctypes.c_uint)]
+    lib.solort_attn_device_status.restype = ctypes.c_int
+    lib.solort_attn_status_string.argtypes = [ctypes.c_int]
+    lib.solort_attn_status_string.restype = ctypes.c_char_p
+    lib.solort_attn_abi_version.argtypes = []
+    lib.solort_attn_abi_version.restype = ctypes.c_int
+    _optional_symbols(lib)
+    _LIB = lib
+    return lib
+
+
+def _optional_symbols(lib: ctypes.CDLL) -> None:
+    """Declare signatures of entry points added after ABI version 1."""
+    P = ctypes.POINTER
+    if hasattr(lib, "solort_attn_prefill"):
+        lib.solort_attn_prefill.argtypes = [P(SolortPrefillArgs), c_vp]
+        lib.solort_attn_prefill.restype = ctypes.c_int
+
+
+class SolortPrefillArgs(ctypes.Structure):
+    """Mirror of ``SolortPrefillArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("q", c_vp),
+        ("q_stride_token", c_i64), ("q_stride_head", c_i64),
+        ("k", c_vp),
+        ("v", c_vp),
+        ("kv_stride_token", c_i64), ("kv_stride_head", c_i64),
+        ("out", c_vp),
+        ("out_stride_token", c_i64), ("out_stride_head", c_i64),
+        ("q_len", c_i32), ("kv_len", c_i32),
+        ("num_qo_heads", c_i32), ("num_kv_heads", c_i32), ("head_dim", c_i32),
+        ("causal", c_i32),
+        ("scale", c_f32),
+    ]
+
+
+def status_string(code: int) -> str:
+    lib = load()
+    return f"{STATUS_NAMES.get(code, code)}: {lib.solort_attn_status_string(code).decode()}"
+
+
+def check(code: int, what: str) -> None:
+    if code != SOLORT_OK:
+        raise RuntimeError(f"{what} failed: {status_string(code)}")
