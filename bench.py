@@ -364,7 +364,7 @@ def run_gpu_arm(args) -> None:
         "pct_of_8TBs": round(100 * value / world / 8000, 2),
         "roofline": {
             "bound": "hbm",
-            "kernel": "one attention call = decode_kernel (split-KV) + lse_merge_kernel",
+            "kernel": "one attention call = decode_kernel (split-KV) + merge_kernel (PDL-chained)",
             "achieved": round(achieved, 1),
             "peak": peaks[0],
             "unit": "GB/s",

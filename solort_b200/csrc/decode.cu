@@ -1,19 +1,28 @@
-// Split-KV GQA decode / verify for sm_100a, static or paged KV, plus the log-sum-exp merge.
+// Split-KV GQA decode / verify for sm_100a, static or paged KV, with the log-sum-exp merge.
 //
-// One CTA handles one (key split, KV head, sequence). Its KV rows stream through a 3-stage ring
-// of 32 KB shared-memory stages (64 tokens of K and V, two 64-dim halves each) filled by TMA tile
-// loads with 128-byte swizzle; one elected thread issues them and an mbarrier per stage counts
-// the bytes in. Every query row that reads this KV head -- the `group` heads of the group times
-// q_len tokens (up to 32 rows) -- is packed into m16 tensor-core tiles, so each K/V byte is read
-// from HBM once and from shared memory once for all of them: nothing is expanded with
-// repeat_interleave. Four warps take 16-token slices of each stage; QK^T and PV run on mma.sync
-// (bf16 in, fp32 accumulate) with an fp32 online softmax in the exp2 domain whose row max is a
-// quad shuffle. Warps combine through shared memory at the end; each CTA writes either the final
-// bf16 rows (one split) or an fp32 partial (O, LSE) that the merge kernel combines.
+// decode_kernel: one CTA per (key split, KV head, sequence). Its KV rows stream through a 3-stage
+// ring of 32 KB shared-memory stages (64 tokens of K and V, two 64-dim halves each) filled by TMA
+// tile loads (32-row boxes, 128-byte swizzle, only the boxes that hold keys of this split); one
+// thread issues them and an mbarrier per stage counts the bytes in. Every query row that reads this
+// KV head -- the `group` heads of the group times q_len tokens, up to 32 rows -- is packed into m16
+// tensor-core tiles, so each K/V byte is read from HBM once and from shared memory once for all of
+// them: nothing is expanded with repeat_interleave. Four warps take 16-token slices of each stage;
+// QK^T and PV run on mma.sync (bf16 in, fp32 accumulate) with an fp32 online softmax in the exp2
+// domain whose row max is a quad shuffle. The warps combine through shared memory; with one split
+// the CTA writes the final rows, otherwise an fp32 partial (O, LSE) per row.
 //
-// Semantics follow the reference's decode (src/solort/model/cuda_graph_executor.py:168,180-184:
-// keys 0..pos visible), verify (:250: query i at vpos0+i sees keys <= vpos0+i) and the paged
-// addressing of src/solort/cache/kv_cache.py:136-149 (slot = block_table[pos // P] * P + pos % P).
+// merge_kernel: one CTA per output row; its threads split the partials between eight warps and
+// issue every load of the row at once, then combine the warps' (max, sum, O) in shared memory.
+//
+// Both kernels are launched as programmatic dependents (PDL): each lets the next launch begin
+// at its start and waits for its predecessor's completion (griddepcontrol.wait) before its first
+// global-memory access, so launch latency and set-up overlap the previous kernel's tail while all
+// data dependencies keep plain stream order.
+//
+// Splits are sized so the decode grid is two CTAs per SM. Semantics follow the reference's decode
+// (src/solort/model/cuda_graph_executor.py:168,180-184: keys 0..pos visible), verify (:250: query
+// i at vpos0+i sees keys <= vpos0+i) and the paged addressing of src/solort/cache/kv_cache.py:
+// 136-149 (slot = block_table[pos // P] * P + pos % P).
 #include <math.h>
 
 #include "common.cuh"
@@ -27,23 +36,28 @@ namespace dec {
 
 constexpr int kHD = 128;
 constexpr int kTile = 64;                   // tokens per stage
-constexpr int kHalfBytes = kTile * 128;     // 64 tokens x 64 dims bf16 (one swizzled box)
+constexpr int kBox = 32;                    // token rows per TMA box (static caches)
+constexpr int kHalfBytes = kTile * 128;     // 64 tokens x 64 dims bf16
 constexpr int kKVBytes = 2 * kHalfBytes;    // one of K or V for a stage: 16 KB
 constexpr int kStageBytes = 2 * kKVBytes;   // K + V: 32 KB
 constexpr int kStages = 3;
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
-constexpr int kMaxChunk = 4096;             // tokens per split at most
+constexpr int kMaxPagedChunk = 16384;       // tokens per split at most with a block table
+constexpr int kMergeWarps = 8;
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct Params {
   const bf16* q;
   int64_t q_sb, q_st, q_sh;
+  // final output: bf16 rows, or fp32 rows + LSE when out_f32 != nullptr
   bf16* out;
   int64_t o_sb, o_st, o_sh;
-  float* part_o;    // [S][rows_total][hd]
-  float* part_lse;  // [S][rows_total]
-  int write_bf16;   // 1: final bf16 rows (single split); 0: fp32 partial rows
+  float* out_f32;
+  float* lse_out;
+  // split partials (num_splits > 1): [S][rows_total][hd] and [S][rows_total]
+  float* part_o;
+  float* part_lse;
   const int64_t* q_pos;
   const int32_t* q_lens;
   int64_t kv_pos_offset;
@@ -61,6 +75,32 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Write one 4-dim chunk of a finished row (row index R over all rows = (b, token, head)).
+__device__ __forceinline__ void write_final(const Params& p, int R, int c, float4 v, float lse) {
+  if (p.out_f32) {
+    *reinterpret_cast<float4*>(p.out_f32 + static_cast<int64_t>(R) * kHD + c) = v;
+    if (c == 0) p.lse_out[R] = lse;
+  } else {
+    const int h = R % p.nh, t = (R / p.nh) % p.q_len, b = R / (p.nh * p.q_len);
+    bf16* o = p.out + b * p.o_sb + t * p.o_st + h * p.o_sh + c;
+    uint2 pk;
+    pk.x = pack_bf16x2(v.x, v.y);
+    pk.y = pack_bf16x2(v.z, v.w);
+    *reinterpret_cast<uint2*>(o) = pk;
+  }
+}
+
+__device__ __forceinline__ void write_partial(const Params& p, int split, int rows_total, int R,
+                                              int c, float4 v, float lse) {
+  *reinterpret_cast<float4*>(p.part_o + (static_cast<int64_t>(split) * rows_total + R) * kHD + c) = v;
+  if (c == 0) p.part_lse[static_cast<int64_t>(split) * rows_total + R] = lse;
+}
+
 template <int MT, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 2)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
@@ -68,8 +108,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* stages = align1024(smem_raw);
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + kStages * kStageBytes);
-  int* abort_flag = reinterpret_cast<int*>(full + kStages);
-  int* bt_s = abort_flag + 2;
+  int* flags = reinterpret_cast<int*>(full + kStages);  // [0] abort
+  int* bt_s = flags + 2;
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
@@ -78,6 +118,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int rows_total = p.batch * p.q_len * p.nh;
+  const bool single = p.num_splits == 1;
+
+  pdl_launch_dependents();
+  if (tid == 0) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    flags[0] = 0;
+    fence_mbarrier_init();
+  }
+  pdl_wait();  // inputs and the workspace may belong to the kernel before this one
 
   const long long qpos = p.q_pos[b];
   const int qlen_b = p.q_lens ? min(p.q_lens[b], p.q_len) : p.q_len;
@@ -90,24 +141,20 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int t_end = min(t_begin + p.chunk, kv_end);
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kTile - 1) / kTile : 0;
 
-  // Output row (within all rows) of query row r of this CTA's group.
-  auto out_row = [&](int r) { return (b * p.q_len + r / p.group) * p.nh + kvh * p.group + r % p.group; };
+  // Row index over all rows of query row r (token r / group, head kvh*group + r % group).
+  auto out_row = [&](int r) {
+    return (b * p.q_len + r / p.group) * p.nh + kvh * p.group + r % p.group;
+  };
 
   if (ntiles == 0) {
-    // Nothing visible in this split: an empty partial (O = 0, LSE = -inf) or, with a single
-    // split, zero rows.
+    // Nothing visible in this split: an empty partial (O = 0, LSE = -inf), or zero final rows.
     for (int idx = tid; idx < rows_b * (kHD / 4); idx += kThreads) {
       const int r = idx / (kHD / 4), c = (idx % (kHD / 4)) * 4;
-      const int qi = r / p.group, h = kvh * p.group + r % p.group;
-      if (p.write_bf16) {
-        bf16* o = p.out + b * p.o_sb + qi * p.o_st + h * p.o_sh + c;
-        *reinterpret_cast<uint2*>(o) = make_uint2(0u, 0u);
-      } else {
-        const int R = out_row(r);
-        float* o = p.part_o + (static_cast<int64_t>(split) * rows_total + R) * kHD + c;
-        *reinterpret_cast<float4*>(o) = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (c == 0) p.part_lse[static_cast<int64_t>(split) * rows_total + R] = -INFINITY;
-      }
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (single)
+        write_final(p, out_row(r), c, z, -INFINITY);
+      else
+        write_partial(p, split, rows_total, out_row(r), c, z, -INFINITY);
     }
     return;
   }
@@ -116,41 +163,37 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (PAGED) {
     lp0 = t_begin >> p.page_shift;
     const int lp1 = (t_end - 1) >> p.page_shift;
-    for (int i = tid; i <= lp1 - lp0; i += kThreads) bt_s[i] = p.block_table[b * p.bt_stride + lp0 + i];
-  }
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
-    abort_flag[0] = 0;
-    fence_mbarrier_init();
+    for (int i = tid; i <= lp1 - lp0; i += kThreads)
+      bt_s[i] = p.block_table[b * p.bt_stride + lp0 + i];
   }
   __syncthreads();
 
+  // Fill stage s with the boxes of tile `it` that hold keys of this split. Rows of the stage past
+  // the split end keep stale contents; they are masked (K) or zeroed (V) below.
   auto issue = [&](int it, int s) {
     uint8_t* Ks = stages + s * kStageBytes;
     uint8_t* Vs = Ks + kKVBytes;
-    mbar_arrive_expect_tx(&full[s], kStageBytes);
     const int t0 = t_begin + it * kTile;
-    if (!PAGED) {
+    const int br = p.box_rows;
+    const int nbox = min(kTile, t_end - t0 + br - 1) / br;  // boxes with at least one key
+    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nbox * br * 128 * 4));
+    for (int j = 0; j < nbox; ++j) {
+      const int tok = t0 + j * br;
+      int c1, c2, c3;
+      if (!PAGED) {
+        c1 = p.tok_coord == 1 ? tok : kvh;
+        c2 = p.tok_coord == 1 ? kvh : tok;
+        c3 = 0;
+      } else {
+        const int row = tok & (p.page_size - 1);
+        c1 = p.tok_coord == 1 ? row : kvh;
+        c2 = p.tok_coord == 1 ? kvh : row;
+        c3 = bt_s[(tok >> p.page_shift) - lp0];
+      }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int c1 = p.tok_coord == 1 ? t0 : kvh;
-        const int c2 = p.tok_coord == 1 ? kvh : t0;
-        tma_load_4d(Ks + h * kHalfBytes, &tmK, &full[s], h * 64, c1, c2, 0);
-        tma_load_4d(Vs + h * kHalfBytes, &tmV, &full[s], h * 64, c1, c2, 0);
-      }
-    } else {
-      for (int j = 0; j < kTile; j += p.box_rows) {
-        const int tok = t0 + j;
-        const int row = tok & (p.page_size - 1);
-        // Pages past the split are addressed out of range: TMA fills zeros, reads nothing.
-        const int page = tok < t_end ? bt_s[(tok >> p.page_shift) - lp0] : p.num_pages;
-        const int c1 = p.tok_coord == 1 ? row : kvh;
-        const int c2 = p.tok_coord == 1 ? kvh : row;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          tma_load_4d(Ks + h * kHalfBytes + j * 128, &tmK, &full[s], h * 64, c1, c2, page);
-          tma_load_4d(Vs + h * kHalfBytes + j * 128, &tmV, &full[s], h * 64, c1, c2, page);
-        }
+        tma_load_4d(Ks + h * kHalfBytes + j * br * 128, &tmK, &full[s], h * 64, c1, c2, c3);
+        tma_load_4d(Vs + h * kHalfBytes + j * br * 128, &tmV, &full[s], h * 64, c1, c2, c3);
       }
     }
   };
@@ -160,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = 0; i < n0; ++i) issue(i, i);
   }
 
-  // Query fragments (A operand, m16k16 per (mt, ks)); rows beyond this sequence's rows are zero.
+  // Query fragments (A operand, m16k16 per (mt, ks)); rows past this sequence's rows are zero.
   uint32_t qa[MT][8][4];
   int lim[MT][2];  // last visible local key of the two rows this lane holds per m-tile
 #pragma unroll
@@ -207,6 +250,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int e = 0; e < 4; ++e) o_acc[mt][n][e] = 0.f;
   }
 
+  // Two independent QK accumulator chains shorten the dependent mma sequence when registers allow.
+  constexpr int kChains = MT == 1 ? 2 : 1;
   const uint32_t stages_u32 = smem_u32(stages);
   bool ok = true;
   int abort_it = -1;
@@ -215,15 +260,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t parity = (it / kStages) & 1;
     if (!mbar_wait(&full[s], parity, &g_decode_status)) {
       ok = false;
-      abort_flag[0] = 1;
+      flags[0] = 1;
     }
     const int tok0 = t_begin + it * kTile + warp * 16;
     if (ok && tok0 < t_end) {
       const uint32_t Ks = stages_u32 + s * kStageBytes;
       const uint32_t Vs = Ks + kKVBytes;
       if (t_end - tok0 < 16) {
-        // Rows past the last key may hold anything (an unfilled page is uninitialised memory);
-        // their P is exactly 0, but 0 * NaN is not, so zero this warp's V rows past the end.
+        // Rows past the last key hold stale or never-written shared memory; their P is exactly
+        // 0, but 0 * NaN is not, so zero this warp's V rows past the end.
         uint8_t* Vg = stages + s * kStageBytes + kKVBytes;
         const int valid = t_end - tok0;
         for (int idx = lane; idx < (16 - valid) * 16; idx += 32) {
@@ -235,13 +280,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         fence_proxy_async_shared();  // order these writes before the stage's next TMA fill
         __syncwarp();
       }
-      float sc[MT][2][4];
+      float sc[kChains][MT][2][4];
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+      for (int ch = 0; ch < kChains; ++ch)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) sc[mt][nt][e] = 0.f;
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[ch][mt][nt][e] = 0.f;
       // S = Q K^T over 128 dims: 8 k-steps, two n8 tiles of tokens.
       {
         const int mi = lane >> 3;
@@ -254,10 +301,18 @@ __global__ void __launch_bounds__(kThreads, 2)
           ldmatrix_x4(b0, b1, b2, b3, Ks + half * kHalfBytes + swz128(trow, chunk));
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
-            mma_bf16_16816(sc[mt][0], qa[mt][ks], b0, b1);
-            mma_bf16_16816(sc[mt][1], qa[mt][ks], b2, b3);
+            mma_bf16_16816(sc[ks % kChains][mt][0], qa[mt][ks], b0, b1);
+            mma_bf16_16816(sc[ks % kChains][mt][1], qa[mt][ks], b2, b3);
           }
         }
+      }
+      if (kChains == 2) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sc[0][mt][nt][e] += sc[kChains - 1][mt][nt][e];
       }
       // Mask, scale to the exp2 domain, online softmax.
       uint32_t pa[MT][4];
@@ -271,9 +326,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
               const int tok = tok0 + nt * 8 + (lane & 3) * 2 + c;
-              float v = sc[mt][nt][hr * 2 + c] * p.scale_log2;
+              float v = sc[0][mt][nt][hr * 2 + c] * p.scale_log2;
               v = tok <= lim[mt][hr] ? v : -INFINITY;
-              sc[mt][nt][hr * 2 + c] = v;
+              sc[0][mt][nt][hr * 2 + c] = v;
               mx = fmaxf(mx, v);
             }
           mx = warp_max_quad(mx);
@@ -285,8 +340,8 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-              const float e = exp2f(sc[mt][nt][hr * 2 + c] - ref);
-              sc[mt][nt][hr * 2 + c] = e;
+              const float e = exp2f(sc[0][mt][nt][hr * 2 + c] - ref);
+              sc[0][mt][nt][hr * 2 + c] = e;
               rs += e;
             }
           l_run[mt][hr] = l_run[mt][hr] * alpha + rs;
@@ -297,10 +352,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             o_acc[mt][n][hr * 2 + 1] *= alpha;
           }
         }
-        pa[mt][0] = pack_bf16x2(sc[mt][0][0], sc[mt][0][1]);
-        pa[mt][1] = pack_bf16x2(sc[mt][0][2], sc[mt][0][3]);
-        pa[mt][2] = pack_bf16x2(sc[mt][1][0], sc[mt][1][1]);
-        pa[mt][3] = pack_bf16x2(sc[mt][1][2], sc[mt][1][3]);
+        pa[mt][0] = pack_bf16x2(sc[0][mt][0][0], sc[0][mt][0][1]);
+        pa[mt][1] = pack_bf16x2(sc[0][mt][0][2], sc[0][mt][0][3]);
+        pa[mt][2] = pack_bf16x2(sc[0][mt][1][0], sc[0][mt][1][1]);
+        pa[mt][3] = pack_bf16x2(sc[0][mt][1][2], sc[0][mt][1][3]);
       }
       // O += P V: V^T fragments via ldmatrix.trans, 16 n8 tiles of dims.
       {
@@ -321,7 +376,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
     }
     __syncthreads();
-    if (abort_flag[0]) {
+    if (flags[0]) {
       abort_it = it;
       break;
     }
@@ -331,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (abort_it >= 0) {
     // A stage never completed within the time limit. Tiles abort_it .. abort_it+kStages-1 may
     // still have copies in flight: give each a bounded wait before the CTA releases its shared
-    // memory, and write nothing.
+    // memory, and write nothing (the status word tells the host).
     if (tid == 0) {
       const int last = min(ntiles, abort_it + kStages);
       for (int t = abort_it; t < last; ++t) {
@@ -353,9 +408,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int hr = 0; hr < 2; ++hr) l_run[mt][hr] = warp_sum_quad(l_run[mt][hr]);
 
   constexpr int kRows = MT * 16;
-  float* red = reinterpret_cast<float*>(stages);            // [warps][kRows][hd]
-  float* ms = red + kWarps * kRows * kHD;                    // [warps][kRows]
-  float* ls = ms + kWarps * kRows;                           // [warps][kRows]
+  constexpr int kRedStride = kHD + 4;  // padded rows: the fragment stores below hit 32 banks
+  float* red = reinterpret_cast<float*>(stages);  // [warps][kRows][kRedStride]
+  float* ms = red + kWarps * kRows * kRedStride;   // [warps][kRows]
+  float* ls = ms + kWarps * kRows;                 // [warps][kRows]
   if ((lane & 3) == 0) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -379,8 +435,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         const int c = n * 8 + (lane & 3) * 2;
-        float2 v = make_float2(o_acc[mt][n][hr * 2] * f, o_acc[mt][n][hr * 2 + 1] * f);
-        *reinterpret_cast<float2*>(red + (warp * kRows + r) * kHD + c) = v;
+        *reinterpret_cast<float2*>(red + (warp * kRows + r) * kRedStride + c) =
+            make_float2(o_acc[mt][n][hr * 2] * f, o_acc[mt][n][hr * 2 + 1] * f);
       }
     }
   __syncthreads();
@@ -396,28 +452,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int w = 0; w < kWarps; ++w) {
       const float mw = ms[w * kRows + r];
       if (mw != -INFINITY) L += ls[w * kRows + r] * exp2f(mw - M);
-      const float4 v = *reinterpret_cast<const float4*>(red + (w * kRows + r) * kHD + c);
+      const float4 v = *reinterpret_cast<const float4*>(red + (w * kRows + r) * kRedStride + c);
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
       acc.w += v.w;
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
-    const int qi = r / p.group, h = kvh * p.group + r % p.group;
-    if (p.write_bf16) {
-      bf16* o = p.out + b * p.o_sb + qi * p.o_st + h * p.o_sh + c;
-      uint2 pk;
-      pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-      pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-      *reinterpret_cast<uint2*>(o) = pk;
-    } else {
-      const int R = out_row(r);
-      float* o = p.part_o + (static_cast<int64_t>(split) * rows_total + R) * kHD + c;
-      *reinterpret_cast<float4*>(o) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-      if (c == 0)
-        p.part_lse[static_cast<int64_t>(split) * rows_total + R] =
-            L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
-    }
+    const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    const float lse = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+    if (single)
+      write_final(p, out_row(r), c, o, lse);
+    else
+      write_partial(p, split, rows_total, out_row(r), c, o, lse);
   }
 }
 
@@ -427,56 +474,92 @@ struct MergeParams {
   const float* lse_parts;
   int64_t lse_part_stride;
   int num_parts;
-  int rows_total, q_len, nh;
-  bf16* out;
-  int64_t o_sb, o_st, o_sh;
-  float* out_f32;
-  float* lse_out;
+  int rows_total;
   const int32_t* q_lens;  // optional: rows whose token index is past q_lens[b] are skipped
+  Params out;             // output fields only (out / out_f32 / lse_out, strides, q_len, nh)
 };
 
-// One warp per output row; lane l owns dims 4l..4l+3.
-__global__ void __launch_bounds__(128) lse_merge_kernel(const MergeParams p) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int R = blockIdx.x * 4 + warp;
-  if (R >= p.rows_total) return;
+// One CTA per output row, 8 warps; warp g takes parts g, g+8, ... and lane l dims 4l..4l+3.
+// Every thread issues all of its loads before using any, so a row costs one round trip.
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergeParams p) {
+  __shared__ float sm_m[kMergeWarps], sm_d[kMergeWarps];
+  __shared__ float4 sm_o[kMergeWarps][32];
+  const int R = blockIdx.x;
+  const int g = threadIdx.x >> 5, lane = threadIdx.x & 31, c = lane * 4;
+  pdl_launch_dependents();
+  pdl_wait();
   if (p.q_lens) {
-    const int t = (R / p.nh) % p.q_len, b = R / (p.nh * p.q_len);
+    const int t = (R / p.out.nh) % p.out.q_len, b = R / (p.out.nh * p.out.q_len);
     if (t >= p.q_lens[b]) return;
   }
-  float mx = -INFINITY;
-  for (int i = lane; i < p.num_parts; i += 32) mx = fmaxf(mx, p.lse_parts[i * p.lse_part_stride + R]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  float m = -INFINITY, den = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  float den = 0.f;
-  if (mx != -INFINITY) {
-    for (int i = 0; i < p.num_parts; ++i) {
-      const float l = p.lse_parts[i * p.lse_part_stride + R];
-      if (l == -INFINITY) continue;
-      const float w = __expf(l - mx);
-      den += w;
-      const float4 v = *reinterpret_cast<const float4*>(p.o_parts + i * p.part_stride +
-                                                        static_cast<int64_t>(R) * kHD + lane * 4);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
+  constexpr int kBatch = 8;  // parts per warp loaded together
+  for (int s0 = g; s0 < p.num_parts; s0 += kMergeWarps * kBatch) {
+    float l[kBatch];
+    float4 v[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int s = s0 + i * kMergeWarps;
+      if (s < p.num_parts) {
+        l[i] = __ldcg(p.lse_parts + s * p.lse_part_stride + R);
+        v[i] = __ldcg(reinterpret_cast<const float4*>(p.o_parts + s * p.part_stride +
+                                                      static_cast<int64_t>(R) * kHD + c));
+      } else {
+        l[i] = -INFINITY;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    float mb = m;
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) mb = fmaxf(mb, l[i]);
+    if (mb != -INFINITY) {
+      const float a = __expf(m - mb);  // m == -inf gives 0: nothing accumulated yet
+      den *= a;
+      acc.x *= a;
+      acc.y *= a;
+      acc.z *= a;
+      acc.w *= a;
+#pragma unroll
+      for (int i = 0; i < kBatch; ++i) {
+        const float w = __expf(l[i] - mb);
+        den += w;
+        acc.x += w * v[i].x;
+        acc.y += w * v[i].y;
+        acc.z += w * v[i].z;
+        acc.w += w * v[i].w;
+      }
+      m = mb;
     }
   }
-  const float inv = den > 0.f ? 1.f / den : 0.f;
-  if (p.out_f32) {
-    *reinterpret_cast<float4*>(p.out_f32 + static_cast<int64_t>(R) * kHD + lane * 4) =
-        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    if (lane == 0) p.lse_out[R] = den > 0.f ? mx + logf(den) : -INFINITY;
-  } else {
-    const int h = R % p.nh, t = (R / p.nh) % p.q_len, b = R / (p.nh * p.q_len);
-    bf16* o = p.out + b * p.o_sb + t * p.o_st + h * p.o_sh + lane * 4;
-    uint2 pk;
-    pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-    pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(o) = pk;
+  if (lane == 0) {
+    sm_m[g] = m;
+    sm_d[g] = den;
   }
+  sm_o[g][lane] = acc;
+  __syncthreads();
+  if (g != 0) return;
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < kMergeWarps; ++w) M = fmaxf(M, sm_m[w]);
+  float D = 0.f;
+  float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (M != -INFINITY) {
+#pragma unroll
+    for (int w = 0; w < kMergeWarps; ++w) {
+      if (sm_m[w] == -INFINITY) continue;
+      const float f = __expf(sm_m[w] - M);
+      const float4 x = sm_o[w][lane];
+      D += sm_d[w] * f;
+      o.x += x.x * f;
+      o.y += x.y * f;
+      o.z += x.z * f;
+      o.w += x.w * f;
+    }
+  }
+  const float inv = D > 0.f ? 1.f / D : 0.f;
+  write_final(p.out, R, c, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
+              D > 0.f ? M + logf(D) : -INFINITY);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -489,12 +572,14 @@ struct Plan {
   int kv_limit = 0;
   int chunk = 0;
   int splits = 0;
+  size_t part_o_bytes = 0;
+  size_t part_lse_bytes = 0;
   size_t ws_bytes = 0;
   size_t smem_bytes = 0;
   int rows_total = 0;
 };
 
-inline int ceil_div(int64_t a, int64_t b) { return static_cast<int>((a + b - 1) / b); }
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 int make_plan(const SolortDecodeArgs* a, Plan* pl) {
   if (!a || !pl) return SOLORT_ERR_INVALID_ARGUMENT;
@@ -521,44 +606,72 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl) {
   DeviceInfo di;
   int rc = current_device_info(&di);
   if (rc != SOLORT_OK) return rc;
-  const int resident = 2 * di.sm_count;
-  const int heads = a->batch * a->num_kv_heads;
-  int target = a->num_splits > 0 ? a->num_splits : (resident / heads > 1 ? resident / heads : 1);
-  int chunk = ceil_div(pl->kv_limit, target);
-  chunk = ceil_div(chunk, kTile) * kTile;
-  if (chunk > kMaxChunk) chunk = kMaxChunk;
-  if (chunk < kTile) chunk = kTile;
-  pl->chunk = chunk;
-  pl->splits = ceil_div(pl->kv_limit, chunk);
-  if (pl->splits > 65535 * 16) return SOLORT_ERR_UNSUPPORTED;
+  // Two CTAs per SM are resident; size the splits so the grid is one such wave.
+  const int64_t resident = 2ll * di.sm_count;
+  const int64_t heads = static_cast<int64_t>(a->batch) * a->num_kv_heads;
+  const int64_t target =
+      a->num_splits > 0 ? a->num_splits : (resident / heads > 1 ? resident / heads : 1);
+  int64_t chunk = ceil_div(ceil_div(pl->kv_limit, target), kBox) * kBox;
+  if (pl->paged && chunk > kMaxPagedChunk) chunk = kMaxPagedChunk;
+  pl->chunk = static_cast<int>(chunk);
+  const int64_t splits = ceil_div(pl->kv_limit, chunk);
+  if (splits > (1ll << 31) - 1) return SOLORT_ERR_UNSUPPORTED;
+  pl->splits = static_cast<int>(splits);
   pl->rows_total = a->batch * a->q_len * a->num_qo_heads;
-  const bool partial_out = a->lse_out != nullptr;
   if (pl->splits > 1) {
-    pl->ws_bytes = align_up(static_cast<size_t>(pl->splits) * pl->rows_total * kHD * 4, 256) +
-                   align_up(static_cast<size_t>(pl->splits) * pl->rows_total * 4, 256);
-  } else {
-    pl->ws_bytes = 0;
+    pl->part_o_bytes = align_up(static_cast<size_t>(pl->splits) * pl->rows_total * kHD * 4, 256);
+    pl->part_lse_bytes = align_up(static_cast<size_t>(pl->splits) * pl->rows_total * 4, 256);
   }
-  (void)partial_out;
-  const int bt_ints = pl->paged ? (chunk / a->page_size + 2) : 0;
+  pl->ws_bytes = pl->part_o_bytes + pl->part_lse_bytes;
+  const int bt_ints = pl->paged ? (pl->chunk / a->page_size + 2) : 0;
   pl->smem_bytes = 1024 + kStages * kStageBytes + kStages * 8 + 8 + bt_ints * 4;
   return SOLORT_OK;
+}
+
+inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                     cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
 }
 
 template <int MT, bool PAGED>
 int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, dim3 grid,
                   size_t smem, cudaStream_t stream) {
-  static int configured_dev_mask = 0;  // one bit per device ordinal < 31
+  static unsigned configured = 0;  // one bit per device ordinal < 32
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 31 && !(configured_dev_mask & (1 << dev))) {
+  if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
+  const size_t max_smem = 1024 + kStages * kStageBytes + 64 + (kMaxPagedChunk / 8 + 2) * 4;
+  if (smem > max_smem) return SOLORT_ERR_UNSUPPORTED;
+  if (dev >= 32 || !(configured & (1u << dev))) {
     if (cudaFuncSetAttribute(decode_kernel<MT, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             1024 + kStages * kStageBytes + 64 + (kMaxChunk / 8 + 2) * 4) !=
-        cudaSuccess)
+                             static_cast<int>(max_smem)) != cudaSuccess ||
+        cudaFuncSetAttribute(decode_kernel<MT, PAGED>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return SOLORT_ERR_CUDA;
-    configured_dev_mask |= 1 << dev;
+    if (dev < 32) configured |= 1u << dev;
   }
-  decode_kernel<MT, PAGED><<<grid, kThreads, smem, stream>>>(tk, tv, prm);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(grid, dim3(kThreads), smem, stream, attr);
+  if (cudaLaunchKernelEx(&cfg, decode_kernel<MT, PAGED>, tk, tv, prm) != cudaSuccess)
+    return SOLORT_ERR_CUDA;
+  return launch_status();
+}
+
+int launch_merge(const MergeParams& mp, cudaStream_t stream) {
+  if (mp.rows_total <= 0) return SOLORT_OK;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg =
+      pdl_config(dim3(mp.rows_total), dim3(kMergeWarps * 32), 0, stream, attr);
+  if (cudaLaunchKernelEx(&cfg, merge_kernel, mp) != cudaSuccess) return SOLORT_ERR_CUDA;
   return launch_status();
 }
 
@@ -574,10 +687,10 @@ int build_kv_maps(const SolortDecodeArgs* a, const Plan& pl, CUtensorMap* tk, CU
   int rows_per_box;
   uint64_t tok_extent;
   if (pl.paged) {
-    rows_per_box = a->page_size < kTile ? a->page_size : kTile;
+    rows_per_box = a->page_size < kBox ? a->page_size : kBox;
     tok_extent = static_cast<uint64_t>(a->page_size);
   } else {
-    rows_per_box = kTile;
+    rows_per_box = kBox;
     tok_extent = static_cast<uint64_t>(a->kv_capacity);
   }
   *box_rows = rows_per_box;
@@ -604,13 +717,23 @@ int build_kv_maps(const SolortDecodeArgs* a, const Plan& pl, CUtensorMap* tk, CU
     strides[2] = a->kv_stride_page * 2;
   } else {
     dims[3] = 1;
-    const uint64_t s1 = strides[1] * dims[2];
-    strides[2] = (s1 + 15) / 16 * 16;
+    strides[2] = align_up(strides[1] * dims[2], 16);
   }
   box[3] = 1;
   int rc = encode_bf16_map(tk, a->k, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc != SOLORT_OK) return rc;
   return encode_bf16_map(tv, a->v, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+void fill_output_fields(const SolortDecodeArgs* a, Params* prm) {
+  prm->out = static_cast<bf16*>(a->out);
+  prm->o_sb = a->out_stride_batch;
+  prm->o_st = a->out_stride_token;
+  prm->o_sh = a->out_stride_head;
+  prm->out_f32 = a->lse_out ? a->out_f32 : nullptr;
+  prm->lse_out = a->lse_out;
+  prm->q_len = a->q_len;
+  prm->nh = a->num_qo_heads;
 }
 
 }  // namespace dec
@@ -643,11 +766,12 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
   if (partial_out && (!aligned(a->out_f32, 16) || !aligned(a->lse_out, 4)))
     return SOLORT_ERR_INVALID_ARGUMENT;
   if (pl.paged && (!a->block_table || a->block_table_stride <= 0)) return SOLORT_ERR_INVALID_ARGUMENT;
-  if (pl.ws_bytes > 0 && (!a->workspace || a->workspace_bytes < pl.ws_bytes || !aligned(a->workspace, 256)))
+  if (pl.ws_bytes > 0 &&
+      (!a->workspace || a->workspace_bytes < pl.ws_bytes || !aligned(a->workspace, 256)))
     return SOLORT_ERR_WORKSPACE;
 
   CUtensorMap tk, tv;
-  int tok_coord = 1, box_rows = kTile;
+  int tok_coord = 1, box_rows = kBox;
   rc = build_kv_maps(a, pl, &tk, &tv, &tok_coord, &box_rows);
   if (rc != SOLORT_OK) return rc;
 
@@ -656,25 +780,11 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
   prm.q_sb = a->q_stride_batch;
   prm.q_st = a->q_stride_token;
   prm.q_sh = a->q_stride_head;
-  prm.out = static_cast<bf16*>(a->out);
-  prm.o_sb = a->out_stride_batch;
-  prm.o_st = a->out_stride_token;
-  prm.o_sh = a->out_stride_head;
-  float* ws_o = nullptr;
-  float* ws_l = nullptr;
+  fill_output_fields(a, &prm);
   if (pl.splits > 1) {
-    ws_o = static_cast<float*>(a->workspace);
-    ws_l = reinterpret_cast<float*>(static_cast<uint8_t*>(a->workspace) +
-                                    align_up(static_cast<size_t>(pl.splits) * pl.rows_total * kHD * 4, 256));
-    prm.part_o = ws_o;
-    prm.part_lse = ws_l;
-    prm.write_bf16 = 0;
-  } else if (partial_out) {
-    prm.part_o = a->out_f32;
-    prm.part_lse = a->lse_out;
-    prm.write_bf16 = 0;
-  } else {
-    prm.write_bf16 = 1;
+    uint8_t* ws = static_cast<uint8_t*>(a->workspace);
+    prm.part_o = reinterpret_cast<float*>(ws);
+    prm.part_lse = reinterpret_cast<float*>(ws + pl.part_o_bytes);
   }
   prm.q_pos = a->q_pos;
   prm.q_lens = a->q_lens;
@@ -690,8 +800,6 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
   prm.tok_coord = tok_coord;
   prm.kv_limit = pl.kv_limit;
   prm.batch = a->batch;
-  prm.q_len = a->q_len;
-  prm.nh = a->num_qo_heads;
   prm.nkv = a->num_kv_heads;
   prm.group = a->num_qo_heads / a->num_kv_heads;
   prm.chunk = pl.chunk;
@@ -707,28 +815,17 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
     rc = pl.paged ? launch_decode<2, true>(tk, tv, prm, grid, pl.smem_bytes, stream)
                   : launch_decode<2, false>(tk, tv, prm, grid, pl.smem_bytes, stream);
   }
-  if (rc != SOLORT_OK) return rc;
-  if (pl.splits > 1) {
-    MergeParams mp{};
-    mp.o_parts = ws_o;
-    mp.part_stride = static_cast<int64_t>(pl.rows_total) * kHD;
-    mp.lse_parts = ws_l;
-    mp.lse_part_stride = pl.rows_total;
-    mp.num_parts = pl.splits;
-    mp.rows_total = pl.rows_total;
-    mp.q_len = a->q_len;
-    mp.nh = a->num_qo_heads;
-    mp.out = static_cast<bf16*>(a->out);
-    mp.o_sb = a->out_stride_batch;
-    mp.o_st = a->out_stride_token;
-    mp.o_sh = a->out_stride_head;
-    mp.out_f32 = partial_out ? a->out_f32 : nullptr;
-    mp.lse_out = partial_out ? a->lse_out : nullptr;
-    mp.q_lens = a->q_lens;
-    lse_merge_kernel<<<ceil_div(pl.rows_total, 4), 128, 0, stream>>>(mp);
-    rc = launch_status();
-  }
-  return rc;
+  if (rc != SOLORT_OK || pl.splits == 1) return rc;
+  MergeParams mp{};
+  mp.o_parts = prm.part_o;
+  mp.part_stride = static_cast<int64_t>(pl.rows_total) * kHD;
+  mp.lse_parts = prm.part_lse;
+  mp.lse_part_stride = pl.rows_total;
+  mp.num_parts = pl.splits;
+  mp.rows_total = pl.rows_total;
+  mp.q_lens = a->q_lens;
+  fill_output_fields(a, &mp.out);
+  return launch_merge(mp, stream);
 }
 
 extern "C" int solort_attn_lse_merge(const SolortMergeArgs* a, void* stream_v) {
@@ -742,6 +839,8 @@ extern "C" int solort_attn_lse_merge(const SolortMergeArgs* a, void* stream_v) {
   if (!a->out_f32 &&
       (!aligned(a->out, 8) || (a->out_stride_batch | a->out_stride_token | a->out_stride_head) & 3))
     return SOLORT_ERR_INVALID_ARGUMENT;
+  const int64_t rows = static_cast<int64_t>(a->batch) * a->q_len * a->num_qo_heads;
+  if (rows > (1ll << 31) - 1) return SOLORT_ERR_UNSUPPORTED;
   DeviceInfo di;
   int rc = current_device_info(&di);
   if (rc != SOLORT_OK) return rc;
@@ -751,17 +850,17 @@ extern "C" int solort_attn_lse_merge(const SolortMergeArgs* a, void* stream_v) {
   mp.lse_parts = a->lse_parts;
   mp.lse_part_stride = a->lse_part_stride;
   mp.num_parts = a->num_parts;
-  mp.rows_total = a->batch * a->q_len * a->num_qo_heads;
-  mp.q_len = a->q_len;
-  mp.nh = a->num_qo_heads;
-  mp.out = static_cast<bf16*>(a->out);
-  mp.o_sb = a->out_stride_batch;
-  mp.o_st = a->out_stride_token;
-  mp.o_sh = a->out_stride_head;
-  mp.out_f32 = a->out_f32;
-  mp.lse_out = a->lse_out;
-  lse_merge_kernel<<<ceil_div(mp.rows_total, 4), 128, 0, static_cast<cudaStream_t>(stream_v)>>>(mp);
-  return launch_status();
+  mp.rows_total = static_cast<int>(rows);
+  mp.q_lens = nullptr;
+  mp.out.out = static_cast<bf16*>(a->out);
+  mp.out.o_sb = a->out_stride_batch;
+  mp.out.o_st = a->out_stride_token;
+  mp.out.o_sh = a->out_stride_head;
+  mp.out.out_f32 = a->out_f32;
+  mp.out.lse_out = a->lse_out;
+  mp.out.q_len = a->q_len;
+  mp.out.nh = a->num_qo_heads;
+  return launch_merge(mp, static_cast<cudaStream_t>(stream_v));
 }
 
 namespace solort {
