@@ -47,6 +47,7 @@ extern "C" {
 #define SOLORT_ERR_CUDA (-4)             /* a CUDA runtime call or kernel launch failed */
 #define SOLORT_ERR_TENSOR_MAP (-5)       /* the driver rejected a TMA descriptor */
 #define SOLORT_ERR_NO_DEVICE (-6)        /* no sm_100 device is current */
+#define SOLORT_ERR_SCRATCH_LIMIT (-7)    /* the call needs more split scratch than the static 4 MiB */
 
 /*
  * GQA attention of q_len query tokens per sequence against a KV cache: decode (q_len == 1),
@@ -111,6 +112,27 @@ typedef struct SolortDecodeArgs {
 
 SOLORT_API int solort_attn_decode_workspace_size(const SolortDecodeArgs* args, size_t* bytes);
 SOLORT_API int solort_attn_decode(const SolortDecodeArgs* args, void* stream);
+
+/*
+ * solort_attn_decode for callers that cannot allocate device memory. It has no counterpart in the
+ * reference. Some callers have no way to provide a workspace: a plugin host whose operator
+ * interface passes only input and output buffers, or a host runtime that binds this C ABI but has
+ * no CUDA allocator of its own. This entry point takes the same arguments, ignores `workspace` /
+ * `workspace_bytes`, and keeps the split partials in a 4 MiB device array inside the library
+ * instead; it calls no allocator.
+ *
+ *  - Limit: calls whose split partials need more than 4 MiB (solort_attn_decode_workspace_size)
+ *    are rejected with SOLORT_ERR_SCRATCH_LIMIT; use solort_attn_decode with a workspace for them.
+ *    Decode of one sequence with 32 query heads needs about 0.6 MiB.
+ *  - The array is allocated once per GPU when the library's device code loads, and stays until the
+ *    process exits.
+ *  - The first call on each device looks up the array's device address (with that device current);
+ *    make that first call before any stream capture on that device.
+ *  - All calls on a GPU share the array and it keeps the last call's contents. Nothing in it needs
+ *    to start at zero (a call writes every part it reads), but calls that overlap on the GPU, for
+ *    example on two streams, race on it: serialise them.
+ */
+SOLORT_API int solort_attn_decode_static_scratch(const SolortDecodeArgs* args, void* stream);
 
 /*
  * Merge num_parts partial results over disjoint key sets into one:

@@ -22,12 +22,14 @@ STATUS_NAMES = {
     -4: "SOLORT_ERR_CUDA",
     -5: "SOLORT_ERR_TENSOR_MAP",
     -6: "SOLORT_ERR_NO_DEVICE",
+    -7: "SOLORT_ERR_SCRATCH_LIMIT",
 }
 
 # Every symbol the header declares; tests check the library exports each one.
 EXPORTED_SYMBOLS = (
     "solort_attn_decode_workspace_size",
     "solort_attn_decode",
+    "solort_attn_decode_static_scratch",
     "solort_attn_lse_merge",
     "solort_attn_device_status",
     "solort_attn_status_string",
@@ -104,6 +106,8 @@ def load() -> ctypes.CDLL:
     lib.solort_attn_decode_workspace_size.restype = ctypes.c_int
     lib.solort_attn_decode.argtypes = [P(SolortDecodeArgs), c_vp]
     lib.solort_attn_decode.restype = ctypes.c_int
+    lib.solort_attn_decode_static_scratch.argtypes = [P(SolortDecodeArgs), c_vp]
+    lib.solort_attn_decode_static_scratch.restype = ctypes.c_int
     lib.solort_attn_lse_merge.argtypes = [P(SolortMergeArgs), c_vp]
     lib.solort_attn_lse_merge.restype = ctypes.c_int
     lib.solort_attn_device_status.argtypes = [P(ctypes.c_uint)]

@@ -24,6 +24,9 @@ extern "C" const char* solort_attn_status_string(int code) {
       return "the driver rejected a TMA tensor map";
     case SOLORT_ERR_NO_DEVICE:
       return "no sm_100 device is current";
+    case SOLORT_ERR_SCRATCH_LIMIT:
+      return "the call needs more split scratch than the library's static 4 MiB array; use "
+             "solort_attn_decode with a workspace";
     default:
       return "unknown status";
   }

@@ -873,3 +873,55 @@ int read_decode_status(unsigned* flags) {
   return SOLORT_OK;
 }
 }  // namespace solort
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free decode entry point.
+//
+// Some callers cannot hand this library a workspace: a plugin host whose operator interface passes
+// only input and output buffers, or a host runtime that binds this ABI but has no access to a CUDA
+// allocator of its own. For them, the split partials live in one file-scope device array, sized
+// once for the whole process. Every GPU that loads the library keeps this array until exit, and
+// all calls on a GPU share it.
+// ------------------------------------------------------------------------------------------
+namespace solort {
+namespace dec {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB of split partials at most
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device. In host code the array's name is only
+// a host-side stand-in, so the address is looked up once per device, with that device current, and
+// cached.
+int static_scratch_address(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SOLORT_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr)
+      return SOLORT_ERR_CUDA;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return SOLORT_OK;
+}
+
+}  // namespace dec
+}  // namespace solort
+
+extern "C" int solort_attn_decode_static_scratch(const SolortDecodeArgs* a, void* stream) {
+  if (!a) return SOLORT_ERR_INVALID_ARGUMENT;
+  size_t need = 0;
+  int rc = solort_attn_decode_workspace_size(a, &need);
+  if (rc != SOLORT_OK) return rc;
+  if (need > kStaticScratchBytes) return SOLORT_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  rc = static_scratch_address(&scratch);  // the first call on a device does this set-up
+  if (rc != SOLORT_OK) return rc;
+  SolortDecodeArgs with_scratch = *a;
+  with_scratch.workspace = scratch;
+  with_scratch.workspace_bytes = kStaticScratchBytes;
+  return solort_attn_decode(&with_scratch, stream);
+}
