@@ -158,6 +158,32 @@ typedef struct SolortMergeArgs {
 
 SOLORT_API int solort_attn_lse_merge(const SolortMergeArgs* args, void* stream);
 
+/*
+ * Causal (or full) GQA prefill on the tcgen05 tensor cores, one sequence.
+ *   q   [q_len,  num_qo_heads, 128] bf16, element strides (q_stride_token, q_stride_head)
+ *   k,v [kv_len, num_kv_heads, 128] bf16, element strides (kv_stride_token, kv_stride_head)
+ *   out [q_len,  num_qo_heads, 128] bf16, element strides (out_stride_token, out_stride_head)
+ * Strides must be multiples of 8 elements and pointers 16-byte aligned (TMA). With causal != 0,
+ * query i attends keys j <= kv_len - q_len + i (bottom-right alignment; q_len <= kv_len): the
+ * square causal prefill when q_len == kv_len. Query head h reads KV head h / (nqo / nkv).
+ * Replaces src/solort/model/cuda_graph_executor.py:124-130 (repeat_interleave + causal SDPA) and
+ * src/solort/backends/transformers_flashinfer.py:114-129 (FlashInfer single_prefill, causal).
+ */
+typedef struct SolortPrefillArgs {
+  const void* q;
+  int64_t q_stride_token, q_stride_head;
+  const void* k;
+  const void* v;
+  int64_t kv_stride_token, kv_stride_head;
+  void* out;
+  int64_t out_stride_token, out_stride_head;
+  int32_t q_len, kv_len, num_qo_heads, num_kv_heads, head_dim;
+  int32_t causal;
+  float scale;
+} SolortPrefillArgs;
+
+SOLORT_API int solort_attn_prefill(const SolortPrefillArgs* args, void* stream);
+
 /* Reads and clears the device status word of the current device (bit 0: an in-kernel wait hit
  * its time limit and the kernel returned without writing its output). */
 SOLORT_API int solort_attn_device_status(unsigned* flags);

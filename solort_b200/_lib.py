@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "solort_attn_decode",
     "solort_attn_decode_static_scratch",
     "solort_attn_lse_merge",
+    "solort_attn_prefill",
     "solort_attn_device_status",
     "solort_attn_status_string",
     "solort_attn_abi_version",
@@ -122,11 +123,9 @@ def load() -> ctypes.CDLL:
 
 
 def _optional_symbols(lib: ctypes.CDLL) -> None:
-    """Declare signatures of entry points added after ABI version 1."""
     P = ctypes.POINTER
-    if hasattr(lib, "solort_attn_prefill"):
-        lib.solort_attn_prefill.argtypes = [P(SolortPrefillArgs), c_vp]
-        lib.solort_attn_prefill.restype = ctypes.c_int
+    lib.solort_attn_prefill.argtypes = [P(SolortPrefillArgs), c_vp]
+    lib.solort_attn_prefill.restype = ctypes.c_int
 
 
 class SolortPrefillArgs(ctypes.Structure):

@@ -1,10 +1,480 @@
-// Causal GQA prefill on tcgen05 (sm_100a). Status word of this translation unit.
+// Causal GQA prefill on the 5th-generation tensor cores (tcgen05 + TMEM) for sm_100a.
+//
+// One CTA computes one 128-row tile of queries for one query head against the KV head of its
+// group (GQA without expanding K/V: the four query heads of a group read the same K/V tiles,
+// which stay in L2). 256 threads with fixed roles:
+//   warp 0, lane 0   TMA: the Q tile once, then K tiles into a 2-stage ring
+//   warp 2, lane 0   TMA: V tiles into a 2-stage ring
+//   warp 1           allocates 512 TMEM columns (S double buffer + O); lane 0 issues every
+//                    tcgen05.mma: S_j = Q K_j^T into S[j&1], then O += P_{j-1} V_{j-1}
+//   warps 4..7       softmax: thread r owns query row r; it reads S row r from TMEM
+//                    (tcgen05.ld 32x32b), keeps the row max / sum in registers, writes P as bf16
+//                    to shared memory in the 128B-swizzled K-major layout the MMA reads, rescales
+//                    its O row in TMEM when its max grows by more than 2^8, and finally normalises
+//                    O and stores the row.
+// Tiles above the causal diagonal are skipped; only diagonal / partial tiles are masked.
+// Completion is tracked with mbarriers (TMA transaction bytes, tcgen05.commit, thread arrivals);
+// every wait is bounded and a shared abort flag lets all roles leave together.
+//
+// Semantics: the reference's causal SDPA over the padded prompt (src/solort/model/
+// cuda_graph_executor.py:124-130) and the HF bridge's bottom-right causal alignment when q_len <
+// kv_len (src/solort/backends/transformers_flashinfer.py:182-193): query i sees keys
+// j <= kv_len - q_len + i.
+#include <math.h>
+
 #include "common.cuh"
 #include "host_util.h"
 
 namespace solort {
 
 __device__ unsigned g_prefill_status;
+
+namespace pre {
+
+constexpr int kHD = 128;
+constexpr int kBM = 128;                     // query rows per CTA
+constexpr int kBN = 128;                     // keys per tile
+constexpr int kTileBytes = kBN * kHD * 2;    // 32 KB: one K or V tile (two 64-dim swizzled halves)
+constexpr int kHalf = kTileBytes / 2;        // 16 KB
+constexpr int kStages = 2;
+constexpr int kThreads = 256;
+constexpr int kTmemCols = 512;
+constexpr float kRescaleLog2 = 8.f;          // lazy rescale threshold (factor 256)
+
+// shared memory map (offsets from a 1024-aligned base)
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTileBytes;
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffP = kOffV + kStages * kTileBytes;
+constexpr int kOffBar = kOffP + kTileBytes;
+constexpr int kSmemBytes = 1024 + kOffBar + 256;
+
+struct Params {
+  bf16* out;
+  int64_t o_st, o_sh;
+  int q_len, kv_len, nh, group;
+  int q_tiles;
+  int causal;
+  int q_tok_coord, kv_tok_coord;  // 1: map coords (d, tok, head); 2: (d, head, tok)
+  float scale_log2;
+};
+
+// Barrier indices
+enum {
+  kBarQ = 0,
+  kBarKFull = 1,                  // +stage
+  kBarKEmpty = kBarKFull + kStages,
+  kBarVFull = kBarKEmpty + kStages,
+  kBarVEmpty = kBarVFull + kStages,
+  kBarSFull = kBarVEmpty + kStages,  // +buffer (2)
+  kBarSFree = kBarSFull + 2,         // +buffer (2), 128 arrivals
+  kBarPFull = kBarSFree + 2,         // 128 arrivals
+  kBarPVDone = kBarPFull + 1,
+  kNumBars = kBarPVDone + 1
+};
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;  // descriptor version for sm_100
+  d |= static_cast<uint64_t>(2u) << 61;  // 128-byte swizzle
+  return d;
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, M = 128, N = 128.
+constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((kBN >> 3) << 17) |
+                              ((kBM >> 4) << 24);                // A, B K-major
+constexpr uint32_t kIdescPV = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) |
+                              ((kHD >> 3) << 17) | ((kBM >> 4) << 24);  // B (V) MN-major
+
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// Bounded wait that also gives up as soon as another role has aborted.
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if ((i & 127u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(&g_prefill_status, kDevErrBarrierTimeout);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                   const __grid_constant__ CUtensorMap tmV, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // issue / commit counts, read by the abort drain: [0] K tiles, [1] V tiles, [2] QK, [3] PV
+  volatile int* counts = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  const uint32_t sbase = smem_u32(smem);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // heaviest (last) query tiles first
+  const int q_tile = p.q_tiles - 1 - static_cast<int>(blockIdx.x) / p.nh;
+  const int head = static_cast<int>(blockIdx.x) % p.nh;
+  const int kvh = head / p.group;
+  const int q0 = q_tile * kBM;
+  const int offset = p.kv_len - p.q_len;  // bottom-right alignment
+  const int kv_tiles_all = (p.kv_len + kBN - 1) / kBN;
+  int n_tiles = kv_tiles_all;
+  if (p.causal) {
+    const int last_row = min(q0 + kBM, p.q_len) - 1;
+    const int last_key = offset + last_row;  // >= 0 whenever q_len <= kv_len
+    n_tiles = min(kv_tiles_all, last_key / kBN + 1);
+  }
+
+  if (tid == 0) {
+    for (int i = 0; i < kNumBars; ++i) {
+      const uint32_t count = (i == kBarSFree || i == kBarSFree + 1 || i == kBarPFull) ? 128u : 1u;
+      mbar_init(&bars[i], count);
+    }
+    *abort_flag = 0;
+    for (int i = 0; i < 4; ++i) counts[i] = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + kBN};
+  const uint32_t tO = tmem + 2 * kBN;
+
+  if (warp == 0 && lane == 0) {
+    // ---- Q + K producer ----
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmK);
+    mbar_arrive_expect_tx(&bars[kBarQ], kTileBytes);
+    for (int h = 0; h < 2; ++h) {
+      const int c1 = p.q_tok_coord == 1 ? q0 : head, c2 = p.q_tok_coord == 1 ? head : q0;
+      tma_load_3d(smem + kOffQ + h * kHalf, &tmQ, &bars[kBarQ], h * 64, c1, c2);
+    }
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j % kStages;
+      if (j >= kStages && !wait_bar(&bars[kBarKEmpty + s], ((j / kStages) - 1) & 1, abort_flag)) break;
+      mbar_arrive_expect_tx(&bars[kBarKFull + s], kTileBytes);
+      for (int h = 0; h < 2; ++h) {
+        const int t = j * kBN;
+        const int c1 = p.kv_tok_coord == 1 ? t : kvh, c2 = p.kv_tok_coord == 1 ? kvh : t;
+        tma_load_3d(smem + kOffK + s * kTileBytes + h * kHalf, &tmK, &bars[kBarKFull + s], h * 64,
+                    c1, c2);
+      }
+      counts[0] = j + 1;
+    }
+  } else if (warp == 2 && lane == 0) {
+    // ---- V producer ----
+    prefetch_tensormap(&tmV);
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j % kStages;
+      if (j >= kStages && !wait_bar(&bars[kBarVEmpty + s], ((j / kStages) - 1) & 1, abort_flag)) break;
+      mbar_arrive_expect_tx(&bars[kBarVFull + s], kTileBytes);
+      for (int h = 0; h < 2; ++h) {
+        const int t = j * kBN;
+        const int c1 = p.kv_tok_coord == 1 ? t : kvh, c2 = p.kv_tok_coord == 1 ? kvh : t;
+        tma_load_3d(smem + kOffV + s * kTileBytes + h * kHalf, &tmV, &bars[kBarVFull + s], h * 64,
+                    c1, c2);
+      }
+      counts[1] = j + 1;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    auto issue_pv = [&](int i) -> bool {
+      if (!wait_bar(&bars[kBarPFull], i & 1, abort_flag)) return false;
+      const int s = i % kStages;
+      if (!wait_bar(&bars[kBarVFull + s], (i / kStages) & 1, abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t pa = sbase + kOffP, vb = sbase + kOffV + s * kTileBytes;
+#pragma unroll
+      for (int k = 0; k < kBN / 16; ++k) {
+        // P: K-major, 16 keys = 32 B inside a 128 B row, 64-key halves 16 KB apart.
+        const uint64_t da = smem_desc(pa + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+        // V: MN-major (dims contiguous), 16 keys = two 8-row groups (2 x 1024 B); the two 64-dim
+        // halves are 16 KB apart (leading byte offset).
+        const uint64_t db = smem_desc(vb + k * 2048, kHalf, 1024);
+        mma_f16(tO, da, db, kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
+      }
+      mma_commit(&bars[kBarVEmpty + s]);
+      mma_commit(&bars[kBarPVDone]);
+      counts[3] = i + 1;
+      return true;
+    };
+    bool ok = wait_bar(&bars[kBarQ], 0, abort_flag);
+    for (int j = 0; ok && j < n_tiles; ++j) {
+      const int s = j % kStages, b = j & 1;
+      if (!wait_bar(&bars[kBarKFull + s], (j / kStages) & 1, abort_flag)) break;
+      if (j >= 2 && !wait_bar(&bars[kBarSFree + b], ((j - 2) >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t qa = sbase + kOffQ, kb = sbase + kOffK + s * kTileBytes;
+#pragma unroll
+      for (int k = 0; k < kHD / 16; ++k) {
+        const uint64_t da = smem_desc(qa + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+        const uint64_t db = smem_desc(kb + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+        mma_f16(tS[b], da, db, kIdescQK, k > 0 ? 1u : 0u);
+      }
+      mma_commit(&bars[kBarSFull + b]);
+      mma_commit(&bars[kBarKEmpty + s]);
+      counts[2] = j + 1;
+      if (j >= 1 && !issue_pv(j - 1)) {
+        ok = false;
+        break;
+      }
+    }
+    if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
+  } else if (warp >= 4) {
+    // ---- softmax: thread r owns query row r ----
+    const int r = tid - 128;                       // 0..127, TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>((warp - 4) * 32) << 16;
+    const int qi = q0 + r;                         // query index within the prompt
+    const int row_limit = offset + qi;             // last visible key (causal)
+    float m_used = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    uint8_t* P = smem + kOffP;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      if (!__all_sync(0xffffffffu, wait_bar(&bars[kBarSFull + b], (j >> 1) & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tS[b] + lane_off + c * 32, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+      }
+      tc_fence_before();
+      mbar_arrive(&bars[kBarSFree + b]);
+      const int k0 = j * kBN;
+      const bool need_mask = (p.causal && k0 + kBN - 1 > offset + q0) || (k0 + kBN > p.kv_len);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kBN; ++i) {
+        float x = s[i] * p.scale_log2;
+        if (need_mask) {
+          const int key = k0 + i;
+          const bool vis = key < p.kv_len && (!p.causal || key <= row_limit);
+          x = vis ? x : -INFINITY;
+        }
+        s[i] = x;
+        mx = fmaxf(mx, x);
+      }
+      // P buffer and O are free once the previous PV has completed.
+      if (j >= 1 &&
+          !__all_sync(0xffffffffu, wait_bar(&bars[kBarPVDone], (j - 1) & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float m_new = fmaxf(m_used, mx);
+      const bool grow = m_new > m_used + kRescaleLog2 || m_used == -INFINITY;
+      if (__any_sync(0xffffffffu, grow && j > 0)) {
+        // Rescale this warp's O rows in TMEM to the new maxima (warp-collective TMEM access).
+        const float alpha = (m_used == -INFINITY || m_new == -INFINITY) ? 1.f : exp2f(m_used - m_new);
+#pragma unroll
+        for (int c = 0; c < kHD / 32; ++c) {
+          float v[32];
+          tmem_ld32(tO + lane_off + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st32(tO + lane_off + c * 32, v);
+        }
+        tmem_wait_st();
+        l_sum *= alpha;
+        m_used = m_new;
+      } else if (grow) {
+        m_used = m_new;  // first tile: nothing accumulated yet
+      }
+      const float ref = m_used == -INFINITY ? 0.f : m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBN / 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a0 = exp2f(s[c * 8 + 2 * e] - ref);
+          const float a1 = exp2f(s[c * 8 + 2 * e + 1] - ref);
+          rs += a0 + a1;
+          w[e] = pack_bf16x2(a0, a1);
+        }
+        // 16-byte chunk c of row r: 64-key half c/8, chunk c%8 swizzled by row
+        const int half = c >> 3, ch = c & 7;
+        *reinterpret_cast<uint4*>(P + half * kHalf + r * 128 + ((ch ^ (r & 7)) << 4)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l_sum += rs;
+      fence_proxy_async_shared();  // P is read by the tensor core (async proxy)
+      tc_fence_before();
+      mbar_arrive(&bars[kBarPFull]);
+    }
+    if (ok && n_tiles > 0 &&
+        __all_sync(0xffffffffu, wait_bar(&bars[kBarPVDone], (n_tiles - 1) & 1, abort_flag))) {
+      tc_fence_after();
+      __syncwarp();
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      const bool write = qi < p.q_len;
+      bf16* orow = p.out + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh;
+#pragma unroll
+      for (int c = 0; c < kHD / 32; ++c) {
+        float v[32];
+        tmem_ld32(tO + lane_off + c * 32, v);
+        tmem_wait_ld();
+        if (write) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 pk;
+            pk.x = pack_bf16x2(v[g * 8 + 0] * inv, v[g * 8 + 1] * inv);
+            pk.y = pack_bf16x2(v[g * 8 + 2] * inv, v[g * 8 + 3] * inv);
+            pk.z = pack_bf16x2(v[g * 8 + 4] * inv, v[g * 8 + 5] * inv);
+            pk.w = pack_bf16x2(v[g * 8 + 6] * inv, v[g * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = pk;
+          }
+        }
+      }
+    }
+  }
+
+  // ---- teardown: everyone meets here; on abort, let in-flight async work land first ----
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && tid == 0) {
+    // Let every copy and MMA still in flight land before the CTA releases its shared memory and
+    // TMEM: the newest fill of each stage, the Q fill, and the last QK and PV commits (commits
+    // complete in order, so the last one covers every MMA before it). Bounded like every wait.
+    const unsigned long long t0 = globaltimer_ns();
+    auto drain = [&](uint64_t* bar, uint32_t parity) {
+      while (!mbar_try_wait(smem_u32(bar), parity) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      }
+    };
+    drain(&bars[kBarQ], 0);
+    for (int t = max(0, counts[0] - kStages); t < counts[0]; ++t)
+      drain(&bars[kBarKFull + t % kStages], (t / kStages) & 1);
+    for (int t = max(0, counts[1] - kStages); t < counts[1]; ++t)
+      drain(&bars[kBarVFull + t % kStages], (t / kStages) & 1);
+    if (counts[2] > 0) drain(&bars[kBarSFull + ((counts[2] - 1) & 1)], ((counts[2] - 1) >> 1) & 1);
+    if (counts[3] > 0) drain(&bars[kBarPVDone], (counts[3] - 1) & 1);
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();  // lane 0 ran the MMA role alone: reconverge for the warp-collective dealloc
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+int build_map(CUtensorMap* map, const void* base, int64_t stride_tok, int64_t stride_head,
+              int tokens, int heads, int* tok_coord) {
+  if (stride_tok <= 0 || stride_head <= 0) return SOLORT_ERR_INVALID_ARGUMENT;
+  uint64_t dims[3], strides[2];
+  uint32_t box[3];
+  dims[0] = kHD;
+  box[0] = 64;
+  if (stride_head < stride_tok) {
+    *tok_coord = 2;
+    dims[1] = heads;
+    dims[2] = tokens;
+    strides[0] = stride_head * 2;
+    strides[1] = stride_tok * 2;
+    box[1] = 1;
+    box[2] = 128;
+  } else {
+    *tok_coord = 1;
+    dims[1] = tokens;
+    dims[2] = heads;
+    strides[0] = stride_tok * 2;
+    strides[1] = stride_head * 2;
+    box[1] = 128;
+    box[2] = 1;
+  }
+  return encode_bf16_map(map, base, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace pre
 
 int read_prefill_status(unsigned* flags) {
   unsigned v = 0, zero = 0;
@@ -16,3 +486,57 @@ int read_prefill_status(unsigned* flags) {
 }
 
 }  // namespace solort
+
+using namespace solort;
+using namespace solort::pre;
+
+extern "C" int solort_attn_prefill(const SolortPrefillArgs* a, void* stream_v) {
+  if (!a || !a->q || !a->k || !a->v || !a->out) return SOLORT_ERR_INVALID_ARGUMENT;
+  if (a->head_dim != kHD) return SOLORT_ERR_UNSUPPORTED;
+  if (a->q_len <= 0 || a->kv_len <= 0 || a->num_qo_heads <= 0 || a->num_kv_heads <= 0 ||
+      a->num_qo_heads % a->num_kv_heads != 0)
+    return SOLORT_ERR_INVALID_ARGUMENT;
+  if (a->causal && a->q_len > a->kv_len) return SOLORT_ERR_INVALID_ARGUMENT;
+  if (!aligned(a->out, 16) || (a->out_stride_token & 7) || (a->out_stride_head & 7))
+    return SOLORT_ERR_INVALID_ARGUMENT;
+  DeviceInfo di;
+  int rc = current_device_info(&di);
+  if (rc != SOLORT_OK) return rc;
+  if (di.max_smem_optin < kSmemBytes) return SOLORT_ERR_UNSUPPORTED;
+  CUtensorMap tq, tk, tv;
+  int q_tc = 1, kv_tc = 1, tmp = 1;
+  rc = build_map(&tq, a->q, a->q_stride_token, a->q_stride_head, a->q_len, a->num_qo_heads, &q_tc);
+  if (rc != SOLORT_OK) return rc;
+  rc = build_map(&tk, a->k, a->kv_stride_token, a->kv_stride_head, a->kv_len, a->num_kv_heads,
+                 &kv_tc);
+  if (rc != SOLORT_OK) return rc;
+  rc = build_map(&tv, a->v, a->kv_stride_token, a->kv_stride_head, a->kv_len, a->num_kv_heads, &tmp);
+  if (rc != SOLORT_OK) return rc;
+  Params prm{};
+  prm.out = static_cast<bf16*>(a->out);
+  prm.o_st = a->out_stride_token;
+  prm.o_sh = a->out_stride_head;
+  prm.q_len = a->q_len;
+  prm.kv_len = a->kv_len;
+  prm.nh = a->num_qo_heads;
+  prm.group = a->num_qo_heads / a->num_kv_heads;
+  prm.q_tiles = (a->q_len + kBM - 1) / kBM;
+  prm.causal = a->causal ? 1 : 0;
+  prm.q_tok_coord = q_tc;
+  prm.kv_tok_coord = kv_tc;
+  prm.scale_log2 = a->scale * 1.4426950408889634f;
+  const int64_t grid = static_cast<int64_t>(prm.q_tiles) * a->num_qo_heads;
+  if (grid > (1ll << 31) - 1) return SOLORT_ERR_UNSUPPORTED;
+  static unsigned configured = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
+  if (dev >= 32 || !(configured & (1u << dev))) {
+    if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes) != cudaSuccess)
+      return SOLORT_ERR_CUDA;
+    if (dev < 32) configured |= 1u << dev;
+  }
+  prefill_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes,
+                   static_cast<cudaStream_t>(stream_v)>>>(tq, tk, tv, prm);
+  return launch_status();
+}

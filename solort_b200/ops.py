@@ -342,3 +342,42 @@ def device_status() -> int:
 
 def default_scale(head_dim: int = HEAD_DIM) -> float:
     return 1.0 / math.sqrt(head_dim)
+
+
+def gqa_prefill(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    causal: bool = True,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Causal GQA prefill of one sequence on the tcgen05 tensor cores.
+
+    ``q [q_len, nh, 128]``, ``k, v [kv_len, nkv, 128]`` bf16 (token-major NHD views such as the
+    reference's ``qkv.view(t, heads, hd)``; any token / head strides that are multiples of 8).
+    With ``causal`` query ``i`` sees keys ``j <= kv_len - q_len + i``: the square prompt prefill
+    of ``cuda_graph_executor.py:124-130`` and the HF bridge's bottom-right alignment
+    (``transformers_flashinfer.py:182-193``). Returns ``out [q_len, nh, 128]`` bf16.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _check_cuda(name, t, torch.bfloat16)
+        if t.dim() != 3 or t.shape[-1] != HEAD_DIM or t.stride(-1) != 1:
+            raise RuntimeError(f"{name} must be [tokens, heads, 128] with a contiguous head dim")
+    if k.shape != v.shape or k.stride() != v.stride():
+        raise RuntimeError("k and v must have the same shape and strides")
+    T, H, D = q.shape
+    if out is None:
+        out = torch.empty(T, H, D, dtype=torch.bfloat16, device=q.device)
+    a = _lib.SolortPrefillArgs()
+    a.q, a.q_stride_token, a.q_stride_head = q.data_ptr(), q.stride(0), q.stride(1)
+    a.k, a.v = k.data_ptr(), v.data_ptr()
+    a.kv_stride_token, a.kv_stride_head = k.stride(0), k.stride(1)
+    a.out, a.out_stride_token, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+    a.q_len, a.kv_len, a.num_qo_heads, a.num_kv_heads, a.head_dim = T, k.shape[0], H, k.shape[1], D
+    a.causal = 1 if causal else 0
+    a.scale = float(D ** -0.5 if scale is None else scale)
+    _lib.check(_lib.load().solort_attn_prefill(ctypes.byref(a), ctypes.c_void_p(_stream(q.device))),
+               "solort_attn_prefill")
+    return out

@@ -1,0 +1,86 @@
+"""GPU parity of the tcgen05 prefill kernel against the CPU oracle (max-abs <= 2e-2,
+mean-abs <= 2e-3 against fp32 softmax attention over the same bf16 inputs)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as A
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+def _close(got, ref, what):
+    d = (got.float().cpu() - ref.float().cpu()).abs()
+    assert torch.isfinite(got.float()).all(), f"{what}: non-finite"
+    assert d.max().item() <= MAX_ABS, f"{what}: max-abs {d.max().item():.4g}"
+    assert d.mean().item() <= MEAN_ABS, f"{what}: mean-abs {d.mean().item():.4g}"
+
+
+@pytest.mark.parametrize("T", [1, 17, 128, 200, 256, 511, 1024])
+@pytest.mark.parametrize("nh,nkv", [(32, 8), (16, 8)])
+def test_prefill_causal_square(T, nh, nkv):
+    from solort_b200 import ops
+
+    q, k, v = A.make_attention_inputs(T + nh, nh, nkv, 128, T, T, 0)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, 0)
+    out = ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda())
+    torch.cuda.synchronize()
+    _close(out, ref, f"prefill T={T} {nh}/{nkv}")
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("q_len,kv_len", [(3, 7), (100, 300), (128, 1000), (257, 513)])
+def test_prefill_bottom_right_over_cache(q_len, kv_len):
+    """Chunked prefill / verify over a populated cache: bottom-right causal alignment
+    (transformers_flashinfer.py:182-193)."""
+    from solort_b200 import ops
+
+    q, k, v = A.make_attention_inputs(q_len * 3 + kv_len, 32, 8, 128, q_len, kv_len, kv_len - q_len)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, kv_len - q_len)
+    out = ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda())
+    _close(out, ref, f"bottom-right q={q_len} kv={kv_len}")
+    lit = A.sdpa_bottom_right(q.transpose(0, 1)[None].float(), k.transpose(0, 1)[None].float(),
+                              v.transpose(0, 1)[None].float(), 128 ** -0.5, causal=True)[0]
+    _close(out, lit, "vs the bridge's torch fallback")
+
+
+def test_prefill_non_causal():
+    from solort_b200 import ops
+
+    q, k, v = A.make_attention_inputs(5, 32, 8, 128, 130, 390, 389)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, 10 ** 6)
+    out = ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda(), causal=False)
+    _close(out, ref, "non-causal")
+
+
+def test_prefill_strided_qkv_view():
+    """q/k/v as views into one fused QKV GEMM output, as the reference slices them
+    (cuda_graph_executor.py:115-119)."""
+    from solort_b200 import ops
+
+    T, nh, nkv = 300, 32, 8
+    q, k, v = A.make_attention_inputs(9, nh, nkv, 128, T, T, 0)
+    qkv = torch.cat([q.reshape(T, -1), k.reshape(T, -1), v.reshape(T, -1)], -1).cuda()
+    qv = qkv[:, : nh * 128].view(T, nh, 128)
+    kv_ = qkv[:, nh * 128 : (nh + nkv) * 128].view(T, nkv, 128)
+    vv = qkv[:, (nh + nkv) * 128 :].view(T, nkv, 128)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, 0)
+    _close(ops.gqa_prefill(qv, kv_, vv), ref, "strided views")
+
+
+def test_prefill_golden_runner():
+    """The reference runner's own prefill attention tensors (tests/golden/runner_attention.npz)."""
+    from solort_b200 import ops
+
+    d = np.load("tests/golden/runner_attention.npz")
+    for li in range(2):
+        q = torch.from_numpy(d[f"prefill.l{li}.q"]).to(torch.bfloat16).transpose(0, 1).contiguous()
+        k = torch.from_numpy(d[f"prefill.l{li}.k"]).to(torch.bfloat16).transpose(0, 1).contiguous()
+        v = torch.from_numpy(d[f"prefill.l{li}.v"]).to(torch.bfloat16).transpose(0, 1).contiguous()
+        ref = torch.from_numpy(d[f"prefill.l{li}.out"]).transpose(0, 1)
+        _close(ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda()), ref, f"golden prefill l{li}")
