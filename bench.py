@@ -42,7 +42,11 @@ def parse_args():
     ap.add_argument("--ctx", type=int, default=8192, help="keys per GPU")
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--sweep", action="store_true", help="also time L in {128..8192} (stderr)")
+    ap.add_argument("--sweep", action="store_true", help="also time L in {128..8192}")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                    help="decode: BASELINE config 2 (+ prefill section); prefill: config 3 only")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-T", type=int, nargs="+", default=[512, 1024, 4096])
     return ap.parse_args()
 
 
@@ -381,10 +385,15 @@ def run_gpu_arm(args) -> None:
                 "how": "ops.DecodeCall per layer from Python, pinned H2D of the 36 queries and "
                        "D2H of the 36 outputs inside the timed region"},
         "gpu_launches": LAYERS * (2 if world == 1 else 3) * args.steps,
+        "gpu_launches_note": "timed region: 36 decode_kernel + 36 merge_kernel launches per step",
         "clocks": clk,
     }
     if sweep:
         line["sweep"] = sweep
+    if world == 1 and not args.no_prefill:
+        line["prefill"] = prefill_bench(dev, args.steps, args.warmup, tuple(args.prefill_T))
+        if not args.no_cpu_baseline:
+            line["prefill"]["cpu_reference_ms_T512"] = round(cpu_prefill_ms(512, os.cpu_count() or 1), 2)
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_reference_rate(ctx, args.cpu_sample_s, os.cpu_count() or 1)
     if rank == 0:
@@ -448,13 +457,107 @@ def _sweep(kv, q, qpos_full, ws, dev):
     return res
 
 
-def _peaks():
+def prefill_bench(dev, steps: int, warmup: int, lengths=(512, 1024, 4096)) -> dict:
+    """causal prefill attention of a Qwen3-4B layer, q [T, 32, 128],
+    k/v [T, 8, 128] bf16 (seeded, QK-RMSNorm + RoPE). Calls rotate over input sets that
+    together exceed L2. FLOPs (causal, algorithmic) = 2 * T^2 * hd * nh."""
+    import torch
+
+    from solort_b200 import ops
+
+    res = {}
+    peak, src = _peaks(tensor=True)
+    for T in lengths:
+        set_bytes = T * (NH + 2 * NKV) * HD * 2
+        nsets = max(4, -(-(256 << 20) // set_bytes))
+        sets = []
+        for i in range(nsets):
+            g = torch.Generator(device=dev)
+            g.manual_seed(100 + i)
+            pos = torch.arange(T, device=dev)
+            q = _rope(_rmsnorm(torch.randn(T, NH, HD, generator=g, device=dev).to(torch.bfloat16)),
+                      pos, torch.bfloat16)
+            k = _rope(_rmsnorm(torch.randn(T, NKV, HD, generator=g, device=dev).to(torch.bfloat16)),
+                      pos, torch.bfloat16)
+            v = torch.randn(T, NKV, HD, generator=g, device=dev).to(torch.bfloat16)
+            sets.append((q, k, v, torch.empty_like(q)))
+
+        def run_all():
+            for q, k, v, o in sets:
+                ops.gqa_prefill(q, k, v, out=o)
+
+        run_all()
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run_all()
+        for _ in range(max(3, warmup)):
+            graph.replay()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = max(3, steps // 4)
+        torch.cuda.synchronize(dev)
+        a.record()
+        for _ in range(reps):
+            graph.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+        us = a.elapsed_time(b) * 1e3 / (reps * nsets)
+        flops = 2.0 * T * T * HD * NH
+        tf = flops / (us * 1e-6) / 1e12
+        res[str(T)] = {"us_per_call": round(us, 2), "tflops": round(tf, 1),
+                       "frac_of_peak": round(tf / peak, 4), "gflop": round(flops / 1e9, 3),
+                       "rotating_sets": nsets}
+        del graph, sets
+    res["peak_tflops"] = peak
+    res["peak_source"] = src
+    res["kernel"] = "prefill_kernel (tcgen05.mma M128 N128, TMEM accumulators, TMA-fed)"
+    return res
+
+
+def cpu_prefill_ms(T: int, threads: int) -> float:
+    import torch
+
+    from oracle import attention as A
+
+    torch.set_num_threads(threads)
+    q, k, v = A.make_attention_inputs(3, NH, NKV, HD, T, T, 0)
+    A.prefill_reference(q, k, v, HD ** -0.5)
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < 3.0 or n < 2:
+        A.prefill_reference(q, k, v, HD ** -0.5)
+        n += 1
+    return (time.perf_counter() - t0) / n * 1e3
+
+
+def run_prefill_workload(args) -> None:
+    import torch
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    res = prefill_bench(dev, args.steps, args.warmup, tuple(args.prefill_T))
+    T = str(max(args.prefill_T))
+    line = {"metric": "prefill attn TFLOP/s", "value": res[T]["tflops"], "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(res[T]["us_per_call"] / 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen3-4b causal prefill attention (BASELINE config 3)",
+                       "T": int(T), "num_qo_heads": NH, "num_kv_heads": NKV, "head_dim": HD},
+            "prefill": res}
+    print(json.dumps(line), flush=True)
+
+
+def _peaks(tensor: bool = False):
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as fh:
             d = json.load(fh)
+        if tensor:
+            return float(d["bf16_tflops"]), "measured burst (MEASURED_PEAKS.json bf16_tflops)"
         return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
     except Exception:
+        if tensor:
+            return 1590.0, "fallback 1.59 PFLOP/s"
         return 6650.0, "fallback 6.65 TB/s"
 
 
@@ -462,6 +565,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.workload == "prefill":
+        run_prefill_workload(args)
     else:
         run_gpu_arm(args)
 

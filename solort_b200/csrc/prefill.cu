@@ -1,17 +1,20 @@
 // Causal GQA prefill on the 5th-generation tensor cores (tcgen05 + TMEM) for sm_100a.
 //
 // One CTA computes one 128-row tile of queries for one query head against the KV head of its
-// group (GQA without expanding K/V: the four query heads of a group read the same K/V tiles,
-// which stay in L2). 256 threads with fixed roles:
+// group (GQA without expanding K/V: the query heads of a group read the same K/V tiles, which
+// stay in L2). 384 threads with fixed roles:
 //   warp 0, lane 0   TMA: the Q tile once, then K tiles into a 2-stage ring
 //   warp 2, lane 0   TMA: V tiles into a 2-stage ring
-//   warp 1           allocates 512 TMEM columns (S double buffer + O); lane 0 issues every
-//                    tcgen05.mma: S_j = Q K_j^T into S[j&1], then O += P_{j-1} V_{j-1}
-//   warps 4..7       softmax: thread r owns query row r; it reads S row r from TMEM
-//                    (tcgen05.ld 32x32b), keeps the row max / sum in registers, writes P as bf16
-//                    to shared memory in the 128B-swizzled K-major layout the MMA reads, rescales
-//                    its O row in TMEM when its max grows by more than 2^8, and finally normalises
-//                    O and stores the row.
+//   warp 1           allocates 512 TMEM columns (S/P double buffer + O); lane 0 issues every
+//                    tcgen05.mma: S_j = Q K_j^T into S[j&1] (A, B from shared memory), then
+//                    O += P_{j-1} V_{j-1} with P read from TMEM (A operand in tensor memory)
+//   warps 4..7, 8..11  two softmax warp groups; thread r of group g owns query row r and key
+//                    columns [64g, 64g+64): it reads its S slice from TMEM (tcgen05.ld), the two
+//                    groups exchange row maxima through shared memory, then it writes its slice
+//                    of P as packed bf16 back over S (tcgen05.st), rescales its O columns when
+//                    the row max grows by more than 2^8, and finally normalises and stores O.
+// P aliases the S buffer it came from: the tensor core runs one CTA's MMAs in issue order, and
+// QK_{j+2} (which overwrites that buffer) is issued only after PV_j (which reads P_j).
 // Tiles above the causal diagonal are skipped; only diagonal / partial tiles are masked.
 // Completion is tracked with mbarriers (TMA transaction bytes, tcgen05.commit, thread arrivals);
 // every wait is bounded and a shared abort flag lets all roles leave together.
@@ -37,7 +40,8 @@ constexpr int kBN = 128;                     // keys per tile
 constexpr int kTileBytes = kBN * kHD * 2;    // 32 KB: one K or V tile (two 64-dim swizzled halves)
 constexpr int kHalf = kTileBytes / 2;        // 16 KB
 constexpr int kStages = 2;
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
+constexpr int kSoftmaxThreads = 256;         // two warp groups
 constexpr int kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;          // lazy rescale threshold (factor 256)
 
@@ -45,8 +49,8 @@ constexpr float kRescaleLog2 = 8.f;          // lazy rescale threshold (factor 2
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTileBytes;
 constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffP = kOffV + kStages * kTileBytes;
-constexpr int kOffBar = kOffP + kTileBytes;
+constexpr int kOffX = kOffV + kStages * kTileBytes;  // row-max exchange [2][2][128] + sums [2][128]
+constexpr int kOffBar = kOffX + 3 * 2 * kBM * 4;
 constexpr int kSmemBytes = 1024 + kOffBar + 256;
 
 struct Params {
@@ -62,15 +66,16 @@ struct Params {
 // Barrier indices
 enum {
   kBarQ = 0,
-  kBarKFull = 1,                  // +stage
+  kBarKFull = 1,                     // +stage
   kBarKEmpty = kBarKFull + kStages,
   kBarVFull = kBarKEmpty + kStages,
   kBarVEmpty = kBarVFull + kStages,
-  kBarSFull = kBarVEmpty + kStages,  // +buffer (2)
-  kBarSFree = kBarSFull + 2,         // +buffer (2), 128 arrivals
-  kBarPFull = kBarSFree + 2,         // 128 arrivals
-  kBarPVDone = kBarPFull + 1,
-  kNumBars = kBarPVDone + 1
+  kBarSFull = kBarVEmpty + kStages,  // +buffer (2): QK_j committed
+  kBarPFull = kBarSFull + 2,         // 256 arrivals: P_j written to TMEM
+  kBarPVDone = kBarPFull + 1,        // PV_j committed
+  kBarXMax = kBarPVDone + 1,         // +parity (2), 256 arrivals: row-max exchange
+  kBarXSum = kBarXMax + 2,           // 256 arrivals: final row-sum exchange
+  kNumBars = kBarXSum + 1
 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -96,6 +101,35 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b,
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(d_tmem), "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+// A operand read from tensor memory (K-major: row m in lane m, two 16-bit values per column).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, "
+      "%29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
 }
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -201,7 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
-      const uint32_t count = (i == kBarSFree || i == kBarSFree + 1 || i == kBarPFull) ? 128u : 1u;
+      const uint32_t count =
+          (i == kBarPFull || i == kBarXMax || i == kBarXMax + 1 || i == kBarXSum) ? kSoftmaxThreads : 1u;
       mbar_init(&bars[i], count);
     }
     *abort_flag = 0;
@@ -264,15 +299,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = i % kStages;
       if (!wait_bar(&bars[kBarVFull + s], (i / kStages) & 1, abort_flag)) return false;
       tc_fence_after();
-      const uint32_t pa = sbase + kOffP, vb = sbase + kOffV + s * kTileBytes;
+      const uint32_t vb = sbase + kOffV + s * kTileBytes;
 #pragma unroll
       for (int k = 0; k < kBN / 16; ++k) {
-        // P: K-major, 16 keys = 32 B inside a 128 B row, 64-key halves 16 KB apart.
-        const uint64_t da = smem_desc(pa + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
-        // V: MN-major (dims contiguous), 16 keys = two 8-row groups (2 x 1024 B); the two 64-dim
-        // halves are 16 KB apart (leading byte offset).
+        // P_i in TMEM over S[i&1]: 16 keys = 8 packed columns. V: MN-major (dims contiguous),
+        // 16 keys = two 8-row groups (2 x 1024 B); the 64-dim halves are 16 KB apart.
         const uint64_t db = smem_desc(vb + k * 2048, kHalf, 1024);
-        mma_f16(tO, da, db, kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
+        mma_f16_ts(tO, tS[i & 1] + k * 8, db, kIdescPV, (i > 0 || k > 0) ? 1u : 0u);
       }
       mma_commit(&bars[kBarVEmpty + s]);
       mma_commit(&bars[kBarPVDone]);
@@ -283,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; ok && j < n_tiles; ++j) {
       const int s = j % kStages, b = j & 1;
       if (!wait_bar(&bars[kBarKFull + s], (j / kStages) & 1, abort_flag)) break;
-      if (j >= 2 && !wait_bar(&bars[kBarSFree + b], ((j - 2) >> 1) & 1, abort_flag)) break;
+      // S[b] still holds P_{j-2}; PV_{j-2} was issued before this point, and MMAs run in order.
       tc_fence_after();
       const uint32_t qa = sbase + kOffQ, kb = sbase + kOffK + s * kTileBytes;
 #pragma unroll
@@ -302,14 +335,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && n_tiles > 0) issue_pv(n_tiles - 1);
   } else if (warp >= 4) {
-    // ---- softmax: thread r owns query row r ----
-    const int r = tid - 128;                       // 0..127, TMEM lane
-    const uint32_t lane_off = static_cast<uint32_t>((warp - 4) * 32) << 16;
+    // ---- softmax: group g, thread r owns query row r, key columns [64g, 64g+64) ----
+    const int g = (warp - 4) >> 2;                 // 0 or 1
+    const int r = (tid - 128) & 127;               // TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(((warp - 4) & 3) * 32) << 16;
     const int qi = q0 + r;                         // query index within the prompt
     const int row_limit = offset + qi;             // last visible key (causal)
+    float* xmax = reinterpret_cast<float*>(smem + kOffX);  // [parity][group][row]
+    float* xsum = xmax + 2 * 2 * kBM;                       // [group][row]
     float m_used = -INFINITY, l_sum = 0.f;
     bool ok = true;
-    uint8_t* P = smem + kOffP;
     for (int j = 0; j < n_tiles; ++j) {
       const int b = j & 1;
       if (!__all_sync(0xffffffffu, wait_bar(&bars[kBarSFull + b], (j >> 1) & 1, abort_flag))) {
@@ -317,51 +352,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float s[kBN];
+      float sv[64];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float v[32];
-        tmem_ld32(tS[b] + lane_off + c * 32, v);
+        tmem_ld32(tS[b] + lane_off + 64 * g + c * 32, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = v[i];
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = v[i];
       }
-      tc_fence_before();
-      mbar_arrive(&bars[kBarSFree + b]);
-      const int k0 = j * kBN;
-      const bool need_mask = (p.causal && k0 + kBN - 1 > offset + q0) || (k0 + kBN > p.kv_len);
-      float mx = -INFINITY;
+      const int k0 = j * kBN + 64 * g;
+      const bool need_mask =
+          (p.causal && j * kBN + kBN - 1 > offset + q0) || (j * kBN + kBN > p.kv_len);
+      float mx8[8];
 #pragma unroll
-      for (int i = 0; i < kBN; ++i) {
-        float x = s[i] * p.scale_log2;
+      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        float x = sv[i] * p.scale_log2;
         if (need_mask) {
           const int key = k0 + i;
-          const bool vis = key < p.kv_len && (!p.causal || key <= row_limit);
-          x = vis ? x : -INFINITY;
+          x = (key < p.kv_len && (!p.causal || key <= row_limit)) ? x : -INFINITY;
         }
-        s[i] = x;
-        mx = fmaxf(mx, x);
+        sv[i] = x;
+        mx8[i & 7] = fmaxf(mx8[i & 7], x);
       }
-      // P buffer and O are free once the previous PV has completed.
-      if (j >= 1 &&
-          !__all_sync(0xffffffffu, wait_bar(&bars[kBarPVDone], (j - 1) & 1, abort_flag))) {
+      float pmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                         fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      // exchange partial maxima with the other group (double-buffered by tile parity)
+      xmax[(b * 2 + g) * kBM + r] = pmax;
+      mbar_arrive(&bars[kBarXMax + b]);
+      if (!__all_sync(0xffffffffu, wait_bar(&bars[kBarXMax + b], (j >> 1) & 1, abort_flag))) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      const float m_new = fmaxf(m_used, mx);
-      const bool grow = m_new > m_used + kRescaleLog2 || m_used == -INFINITY;
+      const float row_max = fmaxf(pmax, xmax[(b * 2 + (g ^ 1)) * kBM + r]);
+      const float m_new = fmaxf(m_used, row_max);
+      const bool grow = m_used == -INFINITY || m_new > m_used + kRescaleLog2;
       if (__any_sync(0xffffffffu, grow && j > 0)) {
-        // Rescale this warp's O rows in TMEM to the new maxima (warp-collective TMEM access).
-        const float alpha = (m_used == -INFINITY || m_new == -INFINITY) ? 1.f : exp2f(m_used - m_new);
+        // Rescale this warp's rows of O (our 64 columns) once PV_{j-1} has landed.
+        if (!__all_sync(0xffffffffu, wait_bar(&bars[kBarPVDone], (j - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float alpha =
+            (m_used == -INFINITY || m_new == -INFINITY) ? 1.f : ex2(m_used - m_new);
 #pragma unroll
-        for (int c = 0; c < kHD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           float v[32];
-          tmem_ld32(tO + lane_off + c * 32, v);
+          tmem_ld32(tO + lane_off + 64 * g + c * 32, v);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= alpha;
-          tmem_st32(tO + lane_off + c * 32, v);
+          tmem_st32(tO + lane_off + 64 * g + c * 32, v);
         }
         tmem_wait_st();
         l_sum *= alpha;
@@ -370,48 +414,50 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = m_new;  // first tile: nothing accumulated yet
       }
       const float ref = m_used == -INFINITY ? 0.f : m_used;
-      float rs = 0.f;
+      float rs8[8];
 #pragma unroll
-      for (int c = 0; c < kBN / 8; ++c) {
-        uint32_t w[4];
+      for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+      uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float a0 = exp2f(s[c * 8 + 2 * e] - ref);
-          const float a1 = exp2f(s[c * 8 + 2 * e + 1] - ref);
-          rs += a0 + a1;
-          w[e] = pack_bf16x2(a0, a1);
-        }
-        // 16-byte chunk c of row r: 64-key half c/8, chunk c%8 swizzled by row
-        const int half = c >> 3, ch = c & 7;
-        *reinterpret_cast<uint4*>(P + half * kHalf + r * 128 + ((ch ^ (r & 7)) << 4)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
+      for (int i = 0; i < 32; ++i) {
+        const float a0 = ex2(sv[2 * i] - ref);
+        const float a1 = ex2(sv[2 * i + 1] - ref);
+        rs8[i & 7] += a0 + a1;
+        pk[i] = pack_bf16x2(a0, a1);
       }
-      l_sum += rs;
-      fence_proxy_async_shared();  // P is read by the tensor core (async proxy)
+      l_sum += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      // P slice over S: keys [64g, 64g+64) = packed columns [32g, 32g+32) of buffer b
+      tmem_st32u(tS[b] + lane_off + 32 * g, pk);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars[kBarPFull]);
     }
     if (ok && n_tiles > 0 &&
         __all_sync(0xffffffffu, wait_bar(&bars[kBarPVDone], (n_tiles - 1) & 1, abort_flag))) {
       tc_fence_after();
-      __syncwarp();
-      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      const bool write = qi < p.q_len;
-      bf16* orow = p.out + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh;
+      xsum[g * kBM + r] = l_sum;
+      mbar_arrive(&bars[kBarXSum]);
+      if (__all_sync(0xffffffffu, wait_bar(&bars[kBarXSum], 0, abort_flag))) {
+        const float total = l_sum + xsum[(g ^ 1) * kBM + r];
+        const float inv = total > 0.f ? 1.f / total : 0.f;
+        const bool write = qi < p.q_len;
+        bf16* orow = p.out + static_cast<int64_t>(qi) * p.o_st +
+                     static_cast<int64_t>(head) * p.o_sh + 64 * g;
 #pragma unroll
-      for (int c = 0; c < kHD / 32; ++c) {
-        float v[32];
-        tmem_ld32(tO + lane_off + c * 32, v);
-        tmem_wait_ld();
-        if (write) {
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tmem_ld32(tO + lane_off + 64 * g + c * 32, v);
+          tmem_wait_ld();
+          if (write) {
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 pk;
-            pk.x = pack_bf16x2(v[g * 8 + 0] * inv, v[g * 8 + 1] * inv);
-            pk.y = pack_bf16x2(v[g * 8 + 2] * inv, v[g * 8 + 3] * inv);
-            pk.z = pack_bf16x2(v[g * 8 + 4] * inv, v[g * 8 + 5] * inv);
-            pk.w = pack_bf16x2(v[g * 8 + 6] * inv, v[g * 8 + 7] * inv);
-            *reinterpret_cast<uint4*>(orow + c * 32 + g * 8) = pk;
+            for (int q8 = 0; q8 < 4; ++q8) {
+              uint4 o4;
+              o4.x = pack_bf16x2(v[q8 * 8 + 0] * inv, v[q8 * 8 + 1] * inv);
+              o4.y = pack_bf16x2(v[q8 * 8 + 2] * inv, v[q8 * 8 + 3] * inv);
+              o4.z = pack_bf16x2(v[q8 * 8 + 4] * inv, v[q8 * 8 + 5] * inv);
+              o4.w = pack_bf16x2(v[q8 * 8 + 6] * inv, v[q8 * 8 + 7] * inv);
+              *reinterpret_cast<uint4*>(orow + c * 32 + q8 * 8) = o4;
+            }
           }
         }
       }
