@@ -113,6 +113,26 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       ::"r"(d_tmem), "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
 }
 
+// Packed fp32 pairs (sm_100): one instruction computes two lanes.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t d, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(d));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -361,22 +381,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) sv[c * 32 + i] = v[i];
       }
-      const int k0 = j * kBN + 64 * g;
+      // Raw-score maxima (the scale is positive, so it commutes with max); keys past the causal
+      // limit or the sequence end are -inf. Only diagonal / partial tiles need the mask.
       const bool need_mask =
           (p.causal && j * kBN + kBN - 1 > offset + q0) || (j * kBN + kBN > p.kv_len);
+      if (need_mask) {
+        const int k0 = j * kBN + 64 * g;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const int key = k0 + i;
+          sv[i] = (key < p.kv_len && (!p.causal || key <= row_limit)) ? sv[i] : -INFINITY;
+        }
+      }
       float mx8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        float x = sv[i] * p.scale_log2;
-        if (need_mask) {
-          const int key = k0 + i;
-          x = (key < p.kv_len && (!p.causal || key <= row_limit)) ? x : -INFINITY;
-        }
-        sv[i] = x;
-        mx8[i & 7] = fmaxf(mx8[i & 7], x);
-      }
+      for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
       float pmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       // exchange partial maxima with the other group (double-buffered by tile parity)
@@ -386,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
-      const float row_max = fmaxf(pmax, xmax[(b * 2 + (g ^ 1)) * kBM + r]);
+      const float row_max = fmaxf(pmax, xmax[(b * 2 + (g ^ 1)) * kBM + r]) * p.scale_log2;
       const float m_new = fmaxf(m_used, row_max);
       const bool grow = m_used == -INFINITY || m_new > m_used + kRescaleLog2;
       if (__any_sync(0xffffffffu, grow && j > 0)) {
@@ -414,18 +435,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = m_new;  // first tile: nothing accumulated yet
       }
       const float ref = m_used == -INFINITY ? 0.f : m_used;
-      float rs8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) rs8[i] = 0.f;
+      // p = 2^(s * scale_log2 - ref): one packed FMA per pair, then the exp, sum and bf16 pack.
+      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+      const uint64_t nref2 = f2_pack(-ref, -ref);
+      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float a0 = ex2(sv[2 * i] - ref);
-        const float a1 = ex2(sv[2 * i + 1] - ref);
-        rs8[i & 7] += a0 + a1;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(sv[2 * i], sv[2 * i + 1]), scale2, nref2), x0, x1);
+        const float a0 = ex2(x0), a1 = ex2(x1);
+        sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(a0, a1));
         pk[i] = pack_bf16x2(a0, a1);
       }
-      l_sum += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      {
+        float s0, s1;
+        f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])), s0, s1);
+        l_sum += s0 + s1;
+      }
       // P slice over S: keys [64g, 64g+64) = packed columns [32g, 32g+32) of buffer b
       tmem_st32u(tS[b] + lane_off + 32 * g, pk);
       tmem_wait_st();
