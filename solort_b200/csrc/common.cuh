@@ -86,7 +86,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
 
 // ---------------------------------------------------------------------------------------------
 // TMA (cp.async.bulk.tensor) tile loads, completion counted on an mbarrier. No cluster
-// multicast anywhere in this library.
+// broadcast to other CTAs anywhere in this library: every load fills only its own CTA.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int c0, int c1, int c2, int c3) {

@@ -9,7 +9,7 @@ keys ``[r * S, (r + 1) * S)`` of the sequence in its own HBM. Per layer:
    (``kv_pos_offset``), so causal limits stay exact at shard boundaries.
 2. ``torch.distributed.all_gather_into_tensor`` (NCCL over NVLink / NVSwitch) brings every
    rank's packed partial into this GPU's memory: ``R * rows * 129 * 4`` bytes (16.5 KB per rank
-   for 32 heads). No peer memory is read by a kernel and no cluster-multicast load exists.
+   for 32 heads). No kernel reads peer memory, and every TMA load targets only its own CTA.
 3. ``lse_merge`` combines the ``R`` partials into the bf16 output on every rank.
 
 All buffers are allocated at construction, one set per layer, so a whole decode step (with its
