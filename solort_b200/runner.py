@@ -1,0 +1,267 @@
+"""CUDA-graph Qwen3 runner whose three attention sites run on the engine.
+
+Same public surface and control flow as the reference's ``_GraphQwen3Runner``
+(``src/solort/model/cuda_graph_executor.py:31-289``), so ``CudaGraphQwen3Executor`` and
+``SpecCudaGraphQwen3Executor`` (``:292-482``) can use it unchanged: ``prefill``, ``decode``,
+``decode_argmax``, ``decode_gpu``, ``decode_gpu_argmax``, ``verify``; bucketed decode graphs
+routed by position (``:73-77, 192-214``), bucketed prefill graphs (``:83-85, 137-161``), one
+lazily captured verify graph (``:270-289``); static KV ``[L, max_len, nkv, hd]`` (``:67-69``).
+
+What changes is the attention at the three inline sites:
+* prefill (``:124-130``, ``repeat_interleave`` + causal SDPA) -> ``ops.gqa_prefill`` (tcgen05);
+* decode (``:168, 180-184``, grouped bf16 matmuls over the bucket) -> ``ops.gqa_decode`` reading
+  the live position from ``pos_buf`` on the device (split-KV, fp32 softmax);
+* verify (``:250, 261-263``, ``repeat_interleave`` of the whole buffer + masked SDPA) ->
+  ``ops.gqa_decode`` with ``q_len = K + 1`` (per-row causal limit, no expansion).
+Everything else (weights fusion, norms, RoPE, KV appends, MLP, lm_head, argmax) is the same math
+as the reference, so greedy streams differ only where attention numerics do.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from solort_b200 import ops
+
+
+def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    d = x.float()
+    d = d * torch.rsqrt(d.pow(2).mean(-1, keepdim=True) + eps)
+    return (d * w.float()).to(x.dtype)
+
+
+class GraphQwen3Runner:
+    MAX_VERIFY_TOKENS = 8
+
+    def __init__(self, model, max_len: int) -> None:
+        c = model.config
+        self.dev = next(model.parameters()).device
+        if self.dev.type != "cuda":
+            raise RuntimeError("GraphQwen3Runner requires CUDA")
+        self.dt = model.dtype
+        self.L = int(c.num_hidden_layers)
+        self.nh = int(c.num_attention_heads)
+        self.nkv = int(c.num_key_value_heads)
+        self.hd = int(getattr(c, "head_dim", c.hidden_size // c.num_attention_heads))
+        self.groups = self.nh // self.nkv
+        self.eps = float(c.rms_norm_eps)
+        self.scale = self.hd ** -0.5
+        self.max_len = int(max_len)
+        self.embed = model.model.embed_tokens.weight
+        self.final_norm = model.model.norm.weight
+        self.lm_head = model.lm_head.weight
+        self.q_dim, self.kv_dim = self.nh * self.hd, self.nkv * self.hd
+        self.layers = []
+        for i in range(self.L):
+            a, mlp = model.model.layers[i].self_attn, model.model.layers[i].mlp
+            self.inter = mlp.gate_proj.weight.shape[0]
+            self.layers.append({
+                "in_ln": model.model.layers[i].input_layernorm.weight,
+                "post_ln": model.model.layers[i].post_attention_layernorm.weight,
+                "wqkv": torch.cat([a.q_proj.weight, a.k_proj.weight, a.v_proj.weight], 0).contiguous(),
+                "wo": a.o_proj.weight, "qn": a.q_norm.weight, "kn": a.k_norm.weight,
+                "wgu": torch.cat([mlp.gate_proj.weight, mlp.up_proj.weight], 0).contiguous(),
+                "wd": mlp.down_proj.weight,
+            })
+        theta = float(getattr(c, "rope_theta", None) or c.rope_parameters["rope_theta"])
+        self.inv_freq = 1.0 / (theta ** (torch.arange(0, self.hd, 2, device=self.dev).float() / self.hd))
+        shape = (self.L, self.max_len, self.nkv, self.hd)
+        self.kc = torch.zeros(shape, device=self.dev, dtype=self.dt)
+        self.vc = torch.zeros(shape, device=self.dev, dtype=self.dt)
+        self.tok_buf = torch.zeros(1, dtype=torch.long, device=self.dev)
+        self.pos_buf = torch.zeros(1, dtype=torch.long, device=self.dev)
+        self.buckets = sorted({b for b in (128, 256, 512, 1024, 2048, 4096) if b < self.max_len}
+                              | {self.max_len})
+        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._logits: dict[int, torch.Tensor] = {}
+        self._tok: dict[int, torch.Tensor] = {}
+        self.pre_buckets = sorted({b for b in (16, 32, 64, 128, 256, 512, 1024) if b <= self.max_len})
+        self.pre_tok = torch.zeros(self.max_len, dtype=torch.long, device=self.dev)
+        self._pre_graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._pre_hidden: dict[int, torch.Tensor] = {}
+        self.verify_graph: torch.cuda.CUDAGraph | None = None
+        self.vtok: torch.Tensor | None = None
+        self.vpos0: torch.Tensor | None = None
+        self._vlogits: torch.Tensor | None = None
+        # one split-KV workspace, sized for the largest decode / verify call, allocated before any
+        # graph capture and shared by every layer (calls are stream-ordered)
+        nbytes = max(
+            ops.decode_workspace_bytes(1, q, self.nh, self.nkv, self.max_len, kv_capacity=self.max_len)
+            for q in (1, min(self.MAX_VERIFY_TOKENS, 32 // self.groups))
+        )
+        self.attn_ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=self.dev)
+
+    # ---- shared pieces (same math as the reference) ----
+    def _cos_sin(self, positions: torch.Tensor):
+        f = positions[:, None].float() * self.inv_freq[None, :]
+        emb = torch.cat([f, f], -1)
+        return emb.cos().to(self.dt), emb.sin().to(self.dt)
+
+    @staticmethod
+    def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        d = x.shape[-1] // 2
+        return x * cos + torch.cat([-x[..., d:], x[..., :d]], -1) * sin
+
+    def _qkv(self, x: torch.Tensor, ly: dict, t: int, cos, sin):
+        h = _rmsnorm(x, ly["in_ln"], self.eps)
+        q, k, v = (h @ ly["wqkv"].T).split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
+        q = q.view(t, self.nh, self.hd).transpose(0, 1)
+        k = k.view(t, self.nkv, self.hd).transpose(0, 1)
+        v = v.view(t, self.nkv, self.hd).transpose(0, 1)
+        q = self._rope(_rmsnorm(q, ly["qn"], self.eps), cos, sin)
+        k = self._rope(_rmsnorm(k, ly["kn"], self.eps), cos, sin)
+        return q, k, v  # [heads, t, hd]
+
+    def _mlp(self, x: torch.Tensor, ly: dict) -> torch.Tensor:
+        h2 = _rmsnorm(x, ly["post_ln"], self.eps)
+        gate, up = (h2 @ ly["wgu"].T).split([self.inter, self.inter], dim=-1)
+        return x + (F.silu(gate) * up) @ ly["wd"].T
+
+    # ---- prefill ----
+    def _prefill_forward(self, bound: int) -> torch.Tensor:
+        t = bound
+        cos, sin = self._cos_sin(torch.arange(t, device=self.dev))
+        x = self.embed[self.pre_tok[:bound]].to(self.dt)
+        for li, ly in enumerate(self.layers):
+            q, k, v = self._qkv(x, ly, t, cos, sin)
+            k_t, v_t = k.transpose(0, 1), v.transpose(0, 1)  # [t, nkv, hd]
+            self.kc[li, :t] = k_t
+            self.vc[li, :t] = v_t
+            ctx = ops.gqa_prefill(q.transpose(0, 1), self.kc[li, :t], self.vc[li, :t],
+                                  causal=True, scale=self.scale)
+            x = x + ctx.reshape(t, self.q_dim) @ ly["wo"].T
+            x = self._mlp(x, ly)
+        return _rmsnorm(x, self.final_norm, self.eps)
+
+    def _capture_prefill(self, bound: int) -> None:
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                hid = self._prefill_forward(bound)
+        torch.cuda.current_stream().wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            hid = self._prefill_forward(bound)
+        self._pre_graphs[bound], self._pre_hidden[bound] = graph, hid
+
+    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+        plen = int(ids.shape[0])
+        bound = next(b for b in self.pre_buckets if b >= plen)
+        self.pre_tok[:plen].copy_(ids)
+        self.pre_tok[plen:bound].zero_()
+        if bound not in self._pre_graphs:
+            self._capture_prefill(bound)
+        self._pre_graphs[bound].replay()
+        return (self._pre_hidden[bound][plen - 1: plen] @ self.lm_head.T).float()
+
+    # ---- decode ----
+    def _decode_forward(self, bound: int) -> torch.Tensor:
+        cos, sin = self._cos_sin(self.pos_buf)
+        x = self.embed[self.tok_buf].to(self.dt)
+        for li, ly in enumerate(self.layers):
+            q, k, v = self._qkv(x, ly, 1, cos, sin)
+            self.kc[li].index_copy_(0, self.pos_buf, k.transpose(0, 1))
+            self.vc[li].index_copy_(0, self.pos_buf, v.transpose(0, 1))
+            ctx = ops.gqa_decode(q.reshape(1, 1, self.nh, self.hd), self.kc[li], self.vc[li],
+                                 self.pos_buf, scale=self.scale, max_kv_len=bound,
+                                 workspace=self.attn_ws)
+            x = x + ctx.reshape(1, self.q_dim) @ ly["wo"].T
+            x = self._mlp(x, ly)
+        x = _rmsnorm(x, self.final_norm, self.eps)
+        return (x @ self.lm_head.T).float()
+
+    def _bucket_for(self, pos: int) -> int:
+        return next(b for b in self.buckets if b > pos)
+
+    def _capture(self, bound: int) -> None:
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                lg = self._decode_forward(bound)
+                tk = lg.argmax(-1)
+        torch.cuda.current_stream().wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            lg = self._decode_forward(bound)
+            tk = lg.argmax(-1)
+        self._graphs[bound], self._logits[bound], self._tok[bound] = graph, lg, tk
+
+    def _replay(self, pos: int) -> int:
+        if pos >= self.max_len:
+            raise RuntimeError("decode position exceeds graph_max_len")
+        bound = self._bucket_for(pos)
+        if bound not in self._graphs:
+            self._capture(bound)
+        self._graphs[bound].replay()
+        return bound
+
+    def decode(self, token: int, pos: int) -> torch.Tensor:
+        self.tok_buf.fill_(int(token))
+        self.pos_buf.fill_(int(pos))
+        return self._logits[self._replay(pos)]
+
+    def decode_argmax(self, token: int, pos: int) -> int:
+        self.tok_buf.fill_(int(token))
+        self.pos_buf.fill_(int(pos))
+        return int(self._tok[self._replay(pos)].item())
+
+    def decode_gpu(self, tok_t: torch.Tensor, pos: int) -> torch.Tensor:
+        self.tok_buf.copy_(tok_t.view(1))
+        self.pos_buf.fill_(int(pos))
+        return self._logits[self._replay(pos)].argmax(-1)
+
+    def decode_gpu_argmax(self, tok_t: torch.Tensor, pos: int) -> torch.Tensor:
+        self.tok_buf.copy_(tok_t.view(1))
+        self.pos_buf.fill_(int(pos))
+        return self._tok[self._replay(pos)].clone()
+
+    # ---- verify ----
+    def _verify_forward(self) -> torch.Tensor:
+        k1 = self.vtok.shape[0]
+        pos = self.vpos0 + torch.arange(k1, device=self.dev)
+        cos, sin = self._cos_sin(pos)
+        x = self.embed[self.vtok].to(self.dt)
+        for li, ly in enumerate(self.layers):
+            q, k, v = self._qkv(x, ly, k1, cos, sin)
+            self.kc[li].index_copy_(0, pos, k.transpose(0, 1))
+            self.vc[li].index_copy_(0, pos, v.transpose(0, 1))
+            ctx = ops.gqa_decode(q.transpose(0, 1).reshape(1, k1, self.nh, self.hd), self.kc[li],
+                                 self.vc[li], self.vpos0, scale=self.scale, workspace=self.attn_ws)
+            x = x + ctx.reshape(k1, self.q_dim) @ ly["wo"].T
+            x = self._mlp(x, ly)
+        return (_rmsnorm(x, self.final_norm, self.eps) @ self.lm_head.T).float()
+
+    def verify(self, tok_t: torch.Tensor, pos_start: int) -> torch.Tensor:
+        if self.verify_graph is None:
+            k1 = int(tok_t.shape[0])
+            if k1 * self.groups > 32:
+                raise RuntimeError(f"verify supports at most {32 // self.groups} tokens")
+            self.vtok = torch.zeros(k1, dtype=torch.long, device=self.dev)
+            self.vpos0 = torch.zeros(1, dtype=torch.long, device=self.dev)
+            self.vtok.copy_(tok_t)
+            self.vpos0.fill_(int(pos_start))
+            stream = torch.cuda.Stream()
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    self._vlogits = self._verify_forward()
+            torch.cuda.current_stream().wait_stream(stream)
+            self.verify_graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.verify_graph):
+                self._vlogits = self._verify_forward()
+        self.vtok.copy_(tok_t)
+        self.vpos0.fill_(int(pos_start))
+        self.verify_graph.replay()
+        return self._vlogits
+
+    def greedy(self, prompt: torch.Tensor, steps: int) -> list[int]:
+        """Prefill then ``steps`` greedy tokens through the decode graphs."""
+        toks = [int(self.prefill(prompt).argmax(-1).item())]
+        pos = int(prompt.shape[0])
+        for _ in range(steps):
+            toks.append(self.decode_argmax(toks[-1], pos))
+            pos += 1
+        return toks

@@ -189,3 +189,39 @@ def test_store_gather_round_trip_golden():
     k_out, v_out = OP.gather_layer_tokens(arena, slots)
     assert torch.equal(k_out, torch.from_numpy(d["k_out"]))
     assert torch.equal(v_out, torch.from_numpy(d["v_out"]))
+
+
+def _tiny_model():
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    meta = json.load(open(os.path.join(GOLDEN, "runner_config.json")))
+    keys = ["vocab_size", "hidden_size", "intermediate_size", "num_hidden_layers",
+            "num_attention_heads", "num_key_value_heads", "head_dim", "max_position_embeddings",
+            "rms_norm_eps"]
+    torch.manual_seed(meta["seed"])
+    cfg = Qwen3Config(**{k: meta[k] for k in keys})
+    cfg.rope_parameters = {"rope_type": "default", "rope_theta": 1e6}
+    cfg.rope_theta = 1e6
+    return Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval(), meta
+
+
+def test_oracle_runner_reproduces_reference_runner_stream(runner):
+    """The restated runner (oracle/runner.py) reproduces the reference runner's prefill logits,
+    first decode logits, greedy stream and verify argmax bit-exactly on CPU."""
+    from oracle.runner import ReferenceQwen3Runner
+
+    model, meta = _tiny_model()
+    r = ReferenceQwen3Runner(model, meta["max_len"])
+    prompt = torch.from_numpy(runner["prompt"])
+    with torch.no_grad():
+        lg = r.prefill(prompt)
+        assert torch.equal(lg, torch.from_numpy(runner["prefill.logits"]))
+        toks = [int(lg.argmax(-1))]
+        for step in range(meta["decode_steps"]):
+            dl = r.decode(toks[-1], meta["prompt_len"] + step)
+            if step == 0:
+                assert torch.equal(dl, torch.from_numpy(runner["decode.logits"]))
+            toks.append(int(dl.argmax(-1)))
+        assert toks == runner["tokens"].tolist()
+        vl = r.verify(torch.from_numpy(runner["verify.tokens"]), meta["verify_pos0"])
+        assert vl.argmax(-1).tolist() == runner["verify.argmax"].tolist()
