@@ -125,13 +125,14 @@ def attention_fp32(
     groups = nh // nkv
     kf = k.float().permute(1, 0, 2)  # [nkv, n_kv, hd]
     vf = v.float().permute(1, 0, 2)
-    kpos = kv_pos0 + torch.arange(n_kv)
+    dev = q.device
+    kpos = kv_pos0 + torch.arange(n_kv, device=dev)
     outs, lses = [], []
     for s in range(0, n_q, q_chunk):
         e = min(n_q, s + q_chunk)
         qf = q[s:e].float().permute(1, 0, 2).reshape(nkv, groups * (e - s), hd)
         sc = torch.matmul(qf, kf.transpose(1, 2)).view(nkv, groups, e - s, n_kv) * scale
-        qpos = q_pos0 + torch.arange(s, e)
+        qpos = q_pos0 + torch.arange(s, e, device=dev)
         visible = kpos[None, :] <= qpos[:, None]  # [rows, n_kv]
         sc = sc.masked_fill(~visible.view(1, 1, e - s, n_kv), float("-inf"))
         lse = torch.logsumexp(sc, -1)  # [nkv, g, rows]

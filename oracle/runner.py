@@ -14,11 +14,18 @@ from __future__ import annotations
 import torch
 import torch.nn.functional as F
 
-from oracle.attention import rmsnorm
+from oracle.attention import attention_fp32, rmsnorm
 
 
 class ReferenceQwen3Runner:
-    def __init__(self, model, max_len: int):
+    """``attention="reference"`` (default) runs the reference's literal torch attention;
+    ``attention="fp32"`` swaps in the parity oracle (fp32 softmax over the same bf16 inputs) at the
+    same three sites, everything else unchanged."""
+
+    def __init__(self, model, max_len: int, attention: str = "reference"):
+        if attention not in ("reference", "fp32"):
+            raise ValueError(attention)
+        self.attention = attention
         c = model.config
         self.dev = next(model.parameters()).device
         self.dt = model.dtype
@@ -90,9 +97,14 @@ class ReferenceQwen3Runner:
             k = self._rope(rmsnorm(k, ly["kn"], self.eps), cos, sin)
             self.kc[li, :t] = k.transpose(0, 1)
             self.vc[li, :t] = v.transpose(0, 1)
-            kk = k.repeat_interleave(self.groups, 0)
-            vv = v.repeat_interleave(self.groups, 0)
-            ctx = F.scaled_dot_product_attention(q, kk, vv, is_causal=True, scale=self.scale)
+            if self.attention == "fp32":
+                o, _ = attention_fp32(q.transpose(0, 1), k.transpose(0, 1), v.transpose(0, 1),
+                                      self.scale, 0)
+                ctx = o.to(self.dt).transpose(0, 1)
+            else:
+                kk = k.repeat_interleave(self.groups, 0)
+                vv = v.repeat_interleave(self.groups, 0)
+                ctx = F.scaled_dot_product_attention(q, kk, vv, is_causal=True, scale=self.scale)
             x = x + ctx.transpose(0, 1).reshape(t, self.q_dim) @ ly["wo"].T
             x = self._mlp(x, ly)
         hid = rmsnorm(x, self.final_norm, self.eps)
@@ -115,11 +127,16 @@ class ReferenceQwen3Runner:
             k = self._rope(rmsnorm(k, ly["kn"], self.eps), cos, sin)
             self.kc[li].index_copy_(0, pos_t, k.transpose(0, 1))
             self.vc[li].index_copy_(0, pos_t, v.transpose(0, 1))
-            qg = q.reshape(self.nkv, self.groups, self.hd)
-            kt = self.kc[li, :bound].permute(1, 2, 0)
-            vb = self.vc[li, :bound].permute(1, 0, 2)
-            sc = (torch.matmul(qg, kt) * self.scale).masked_fill(nkeep, float("-inf"))
-            ctx = torch.matmul(torch.softmax(sc, -1).to(self.dt), vb).reshape(1, self.q_dim)
+            if self.attention == "fp32":
+                o, _ = attention_fp32(q.transpose(0, 1), self.kc[li, :bound], self.vc[li, :bound],
+                                      self.scale, pos)
+                ctx = o.to(self.dt).reshape(1, self.q_dim)
+            else:
+                qg = q.reshape(self.nkv, self.groups, self.hd)
+                kt = self.kc[li, :bound].permute(1, 2, 0)
+                vb = self.vc[li, :bound].permute(1, 0, 2)
+                sc = (torch.matmul(qg, kt) * self.scale).masked_fill(nkeep, float("-inf"))
+                ctx = torch.matmul(torch.softmax(sc, -1).to(self.dt), vb).reshape(1, self.q_dim)
             x = x + ctx @ ly["wo"].T
             x = self._mlp(x, ly)
         x = rmsnorm(x, self.final_norm, self.eps)
@@ -142,9 +159,14 @@ class ReferenceQwen3Runner:
             k = self._rope(rmsnorm(k, ly["kn"], self.eps), cos, sin)
             self.kc[li].index_copy_(0, pos, k.transpose(0, 1))
             self.vc[li].index_copy_(0, pos, v.transpose(0, 1))
-            kk = self.kc[li].permute(1, 0, 2).repeat_interleave(self.groups, 0)
-            vv = self.vc[li].permute(1, 0, 2).repeat_interleave(self.groups, 0)
-            ctx = F.scaled_dot_product_attention(q, kk, vv, attn_mask=keep, scale=self.scale)
+            if self.attention == "fp32":
+                o, _ = attention_fp32(q.transpose(0, 1), self.kc[li], self.vc[li], self.scale,
+                                      pos_start)
+                ctx = o.to(self.dt).transpose(0, 1)
+            else:
+                kk = self.kc[li].permute(1, 0, 2).repeat_interleave(self.groups, 0)
+                vv = self.vc[li].permute(1, 0, 2).repeat_interleave(self.groups, 0)
+                ctx = F.scaled_dot_product_attention(q, kk, vv, attn_mask=keep, scale=self.scale)
             x = x + ctx.transpose(0, 1).reshape(k1, self.q_dim) @ ly["wo"].T
             x = self._mlp(x, ly)
         return (rmsnorm(x, self.final_norm, self.eps) @ self.lm_head.T).float()
