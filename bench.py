@@ -47,6 +47,8 @@ def parse_args():
                     help="decode: BASELINE config 2 (+ prefill section); prefill: config 3 only")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-T", type=int, nargs="+", default=[512, 1024, 4096])
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the paged / long-context / tok/s sections of the default line")
     return ap.parse_args()
 
 
@@ -390,6 +392,10 @@ def run_gpu_arm(args) -> None:
     }
     if sweep:
         line["sweep"] = sweep
+    if world == 1 and not args.no_extras:
+        line["paged"] = paged_bench(dev, max(3, args.steps // 4))
+        line["long_ctx"] = long_ctx_bench(dev, max(2, args.steps // 10))
+        line["decode_tok_s"] = tok_s_bench(dev)
     if world == 1 and not args.no_prefill:
         line["prefill"] = prefill_bench(dev, args.steps, args.warmup, tuple(args.prefill_T))
         if not args.no_cpu_baseline:
@@ -511,6 +517,155 @@ def prefill_bench(dev, steps: int, warmup: int, lengths=(512, 1024, 4096)) -> di
     res["peak_tflops"] = peak
     res["peak_source"] = src
     res["kernel"] = "prefill_kernel (tcgen05.mma M128 N128, TMEM accumulators, TMA-fed)"
+    return res
+
+
+def _time_graph(fn, dev, reps: int, warmup: int = 3) -> float:
+    """Capture fn() in a CUDA graph, replay, return ms per replay (CUDA events)."""
+    import torch
+
+    fn()
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    for _ in range(warmup):
+        g.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / reps
+    del g
+    return ms
+
+
+def paged_bench(dev, reps: int) -> dict:
+    """page size 16, context 16384, 36 layers of paged NHD arenas; block tables
+    are a seeded permutation of the physical pages; sequences A and B share their first 4096
+    tokens (256 pages, as a prefix-cache hit gives them). A verifies K = 4 drafts at 16384..16387
+    (each causal over the context and the preceding drafts), B decodes one token at 16383. One
+    call per layer processes both sequences."""
+    import torch
+
+    from solort_b200 import ops
+
+    P, ctx, K, shared = 16, 16384, 4, 256
+    n_a, n_b = ctx + K, ctx
+    pages_a = -(-n_a // P)
+    pages_b = -(-n_b // P)
+    pool = pages_a + pages_b - shared  # 1793 physical pages: A (1025) + B-only (768)
+    g = torch.Generator().manual_seed(4)
+    perm = torch.randperm(pool, generator=g)
+    bt_a = perm[:pages_a]
+    bt_b = torch.cat([bt_a[:shared], perm[pages_a: pages_a + pages_b - shared]])
+    bt = torch.zeros(2, pages_a, dtype=torch.int32)
+    bt[0] = bt_a.to(torch.int32)
+    bt[1, :pages_b] = bt_b.to(torch.int32)
+    bt = bt.to(dev)
+    arenas = []
+    gen = torch.Generator(device=dev)
+    for li in range(LAYERS):
+        gen.manual_seed(500 + li)
+        a = torch.randn(pool, 2, P, NKV, HD, generator=gen, device=dev).to(torch.bfloat16)
+        arenas.append(a)
+    q = torch.zeros(LAYERS, 2, K, NH, HD, dtype=torch.bfloat16, device=dev)
+    q.normal_(generator=gen)
+    qpos = torch.tensor([ctx, ctx - 1], dtype=torch.int64, device=dev)
+    qlens = torch.tensor([K, 1], dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    ws = torch.empty(ops.decode_workspace_bytes(2, K, NH, NKV, n_a, page_size=P), dtype=torch.uint8,
+                     device=dev)
+
+    def step():
+        for li in range(LAYERS):
+            ops.gqa_decode_paged(q[li], arenas[li], bt, qpos, max_kv_len=n_a, q_lens=qlens,
+                                 out=out[li], workspace=ws)
+
+    ms = _time_graph(step, dev, reps)
+    per_layer = (n_a + n_b) * NKV * HD * 2 * 2
+    unique = (n_a + n_b - shared * P) * NKV * HD * 2 * 2
+    us = ms * 1e3 / LAYERS
+    return {"us_per_layer": round(us, 3), "GBs": round(per_layer / (us * 1e-6) / 1e9, 1),
+            "GBs_unique_bytes": round(unique / (us * 1e-6) / 1e9, 1),
+            "bytes_per_layer": per_layer, "unique_bytes_per_layer": unique,
+            "workload": "page 16, ctx 16384, seq A K=4 verify + seq B decode, 256 shared pages, "
+                        "36 layers x 112 MB arenas"}
+
+
+def long_ctx_bench(dev, reps: int, ctx: int = 131072) -> dict:
+    """BASELINE config 5 on one GPU: 32/8 heads, one query at position ctx - 1 over 131072 keys per
+    layer (512 MiB of K+V), 36 layers (18 GiB)."""
+    import torch
+
+    from solort_b200 import ops
+
+    layers = 36
+    kv = torch.empty(layers, 2, NKV, ctx, HD, dtype=torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(77)
+    kv.normal_(generator=gen)
+    q = torch.randn(layers, 1, 1, NH, HD, generator=gen, device=dev).to(torch.bfloat16)
+    qpos = torch.full((1,), ctx - 1, dtype=torch.int64, device=dev)
+    out = torch.empty_like(q)
+    ws = torch.empty(ops.decode_workspace_bytes(1, 1, NH, NKV, ctx), dtype=torch.uint8, device=dev)
+
+    def step():
+        for li in range(layers):
+            ops.gqa_decode(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND", out=out[li],
+                           workspace=ws)
+
+    ms = _time_graph(step, dev, reps)
+    byt = 2 * ctx * NKV * HD * 2
+    us = ms * 1e3 / layers
+    del kv
+    return {"ctx": ctx, "us_per_layer": round(us, 2), "GBs": round(byt / (us * 1e-6) / 1e9, 1),
+            "frac_of_measured_hbm": round(byt / (us * 1e-6) / 1e9 / _peaks()[0], 4)}
+
+
+def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512) -> dict:
+    """End-to-end greedy decode tok/s of the engine's CUDA-graph runner on a random-weight
+    Qwen3-4B-shaped model (36 layers, hidden 2560, 32/8 heads, hd 128, intermediate 9728, vocab
+    151936), the reference microbenchmark's tight loop (decode_gpu_argmax back to back, one sync
+    at the end; scripts/microbench_decode.py:80-84)."""
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+
+    from solort_b200.runner import GraphQwen3Runner
+
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728,
+                      num_hidden_layers=36, num_attention_heads=32, num_key_value_heads=8,
+                      head_dim=128, max_position_embeddings=40960, rms_norm_eps=1e-6,
+                      tie_word_embeddings=True)
+    cfg.rope_parameters = {"rope_type": "default", "rope_theta": 1e6}
+    cfg.rope_theta = 1e6
+    torch.manual_seed(0)
+    with torch.device(dev):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    max_len = prompt_len + new_tokens + 16
+    prompt = torch.randint(0, cfg.vocab_size, (prompt_len,), device=dev)
+    with torch.no_grad():
+        runner = GraphQwen3Runner(model, max_len)
+        first = int(runner.prefill(prompt).argmax(-1).item())
+        cur = first
+        for pos in range(prompt_len, prompt_len + new_tokens + 4):  # capture every bucket
+            cur = runner.decode_argmax(cur, pos)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        tok = torch.tensor([first], device=dev)
+        for pos in range(prompt_len, prompt_len + new_tokens):
+            tok = runner.decode_gpu_argmax(tok, pos)
+        tok.item()
+        dt = time.perf_counter() - t0
+    res = {"tok_s": round(new_tokens / dt, 1), "ms_per_token": round(dt * 1e3 / new_tokens, 3),
+           "model": "random-weight Qwen3-4B shape, bf16", "prompt": prompt_len,
+           "new_tokens": new_tokens,
+           "published_reference_rtx4080_tok_s": 67.0}
+    del runner, model
+    torch.cuda.empty_cache()
     return res
 
 
