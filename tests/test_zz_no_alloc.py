@@ -26,12 +26,12 @@ SCRATCH_LIMIT = 4 << 20
 MAX_ABS, MEAN_ABS = 2e-2, 2e-3
 
 
-def _args(q, k, v, qpos, out, batch_kv=None):
+def _args(q, k, v, qpos, out, num_splits=0):
     return ops._decode_args(
         q, k, v, qpos, stride_token=k.stride(0), stride_head=k.stride(1), stride_page=0,
         kv_capacity=k.shape[0], num_kv_heads=k.shape[1], block_table=None, page_size=0,
         num_pages=0, scale=None, max_kv_len=k.shape[0], out=out, out_f32=None, lse_out=None,
-        q_lens=None, kv_pos_offset=0, num_splits=0)
+        q_lens=None, kv_pos_offset=0, num_splits=num_splits)
 
 
 def _close(got, ref, what):
@@ -44,14 +44,16 @@ def _close(got, ref, what):
 def test_static_scratch_matches_workspace_entry_point_on_two_calls():
     lib = _lib.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    # decode at 8192 keys, then a 5-token verify at 3000: different split counts and row counts
-    for seed, L, q_len in ((1, 8192, 1), (2, 3000, 5)):
+    # decode at 8192 keys, then a 5-token verify at 3000: different split counts and row counts.
+    # An explicit split count keeps the split partials in scratch memory (without it, a single
+    # sequence's splits may merge inside a thread-block cluster and need no scratch at all).
+    for seed, L, q_len, splits in ((1, 8192, 1, 37), (2, 3000, 5, 12)):
         q, k, v = A.make_attention_inputs(seed, 32, 8, 128, q_len, L, L - q_len)
         dq, dk, dv = q[None].cuda(), k.cuda(), v.cuda()
         qpos = torch.tensor([L - q_len], dtype=torch.int64, device="cuda")
 
         out_ref = torch.empty_like(dq)
-        a = _args(dq, dk, dv, qpos, out_ref)
+        a = _args(dq, dk, dv, qpos, out_ref, splits)
         need = ctypes.c_size_t(0)
         assert lib.solort_attn_decode_workspace_size(ctypes.byref(a), ctypes.byref(need)) == 0
         assert 0 < need.value <= SCRATCH_LIMIT
@@ -60,7 +62,7 @@ def test_static_scratch_matches_workspace_entry_point_on_two_calls():
         assert lib.solort_attn_decode(ctypes.byref(a), stream) == 0
 
         out_new = torch.full_like(dq, float("nan"))
-        b = _args(dq, dk, dv, qpos, out_new)
+        b = _args(dq, dk, dv, qpos, out_new, splits)
         b.workspace, b.workspace_bytes = None, 0  # no workspace: the static array is used
         assert lib.solort_attn_decode_static_scratch(ctypes.byref(b), stream) == 0
         torch.cuda.synchronize()
@@ -78,7 +80,7 @@ def test_static_scratch_rejects_calls_beyond_its_limit():
     k = torch.zeros(8192, 8, 128, dtype=torch.bfloat16, device="cuda")
     qpos = torch.zeros(16, dtype=torch.int64, device="cuda")
     out = torch.empty_like(q)
-    a = _args(q, k, k, qpos, out)
+    a = _args(q, k, k, qpos, out, 2)
     need = ctypes.c_size_t(0)
     assert lib.solort_attn_decode_workspace_size(ctypes.byref(a), ctypes.byref(need)) == 0
     assert need.value > SCRATCH_LIMIT
