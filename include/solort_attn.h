@@ -185,7 +185,9 @@ typedef struct SolortPrefillArgs {
 SOLORT_API int solort_attn_prefill(const SolortPrefillArgs* args, void* stream);
 
 /* Reads and clears the device status word of the current device (bit 0: an in-kernel wait hit
- * its time limit and the kernel returned without writing its output). */
+ * its time limit and the kernel returned without writing its output; bit 1: a tensor-memory
+ * allocation wait hit its limit; bit 2: a kernel found its shared memory misaligned and returned
+ * without writing). */
 SOLORT_API int solort_attn_device_status(unsigned* flags);
 
 SOLORT_API const char* solort_attn_status_string(int code);

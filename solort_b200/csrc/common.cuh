@@ -16,6 +16,7 @@ using bf16 = __nv_bfloat16;
 // Device status bits (read and cleared by solort_attn_device_status()).
 constexpr unsigned kDevErrBarrierTimeout = 1u << 0;  // an mbarrier wait ran past its time limit
 constexpr unsigned kDevErrTmemTimeout = 1u << 1;     // a TMEM allocation wait ran past its limit
+constexpr unsigned kDevErrSmemAlign = 1u << 2;       // dynamic shared memory not 1024-aligned
 
 // Upper bound on any single wait inside a kernel, in nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // 1 s

@@ -1,13 +1,14 @@
 // Split-KV GQA decode / verify for sm_100a, static or paged KV, with the log-sum-exp merge.
 //
-// decode_kernel: one CTA per (key split, KV head, sequence). Its KV rows stream through a 3-stage
-// ring of 32 KB shared-memory stages (64 tokens of K and V, two 64-dim halves each) filled by TMA
-// tile loads (32-row boxes, 128-byte swizzle, only the boxes that hold keys of this split); one
-// thread issues them and an mbarrier per stage counts the bytes in. Every query row that reads this
-// KV head -- the `group` heads of the group times q_len tokens, up to 32 rows -- is packed into m16
-// tensor-core tiles, so each K/V byte is read from HBM once and from shared memory once for all of
-// them: nothing is expanded with repeat_interleave. Four warps take 16-token slices of each stage;
-// QK^T and PV run on mma.sync (bf16 in, fp32 accumulate) with an fp32 online softmax in the exp2
+// decode_kernel: one CTA per (key split, KV head, sequence). Its KV rows stream through a 7-stage
+// ring of 16 KB shared-memory stages (32 tokens of K and V, two 64-dim halves each) filled by TMA
+// tile loads (128-byte swizzle, only the boxes that hold keys of this split): 112 KB, so a split
+// of up to 224 keys is requested in full at once and a CTA never waits for its own refill. An
+// mbarrier per stage counts the bytes in. Every query row that reads this KV head -- the `group`
+// heads of the group times q_len tokens, up to 32 rows -- is packed into m16 tensor-core tiles, so
+// each K/V byte is read from HBM once and from shared memory once for all of them: nothing is
+// expanded with repeat_interleave. Warps 0-1 take the even stages and warps 2-3 the odd ones, each
+// warp a 16-token half; the pair that empties a stage refills it. QK^T and PV run on mma.sync (bf16 in, fp32 accumulate) with an fp32 online softmax in the exp2
 // domain whose row max is a quad shuffle. The warps combine through shared memory; with one split
 // the CTA writes the final rows, otherwise an fp32 partial (O, LSE) per row.
 //
@@ -35,14 +36,25 @@ __device__ unsigned g_decode_status;
 namespace dec {
 
 constexpr int kHD = 128;
-constexpr int kTile = 64;                   // tokens per stage
+constexpr int kTile = 32;                   // tokens per stage
 constexpr int kBox = 32;                    // token rows per TMA box (static caches)
-constexpr int kHalfBytes = kTile * 128;     // 64 tokens x 64 dims bf16
-constexpr int kKVBytes = 2 * kHalfBytes;    // one of K or V for a stage: 16 KB
-constexpr int kStageBytes = 2 * kKVBytes;   // K + V: 32 KB
-constexpr int kStages = 3;
-constexpr int kThreads = 128;
-constexpr int kWarps = kThreads / 32;
+constexpr int kHalfBytes = kTile * 128;     // 32 tokens x 64 dims bf16: 4 KB
+constexpr int kKVBytes = 2 * kHalfBytes;    // one of K or V for a stage: 8 KB
+constexpr int kStageBytes = 2 * kKVBytes;   // K + V: 16 KB
+constexpr int kMaxStages = 7;               // 112 KB: a 224-key split is requested at once
+// Two CTAs per SM: 228 KB of shared memory per SM, less 1 KB the hardware keeps per CTA.
+constexpr int kSmemPerCta = 115712;
+// After the ring: full barriers, flags, the tile last issued into each stage, block-table slice.
+constexpr int kHdrBytes = kMaxStages * 8 + 8 + kMaxStages * 4;
+constexpr int kWarps = 4;  // consumer warps (two pairs)
+// Single-tile query blocks (MT == 1) add a fifth warp that only issues the initial TMA fills, so
+// no consumer warp is held up while the copy engine accepts them; MT == 2 needs every register of
+// a 128-thread CTA, so there thread 0 issues them.
+template <int MT>
+struct Shape {
+  static constexpr bool kProducerWarp = MT == 1;
+  static constexpr int kThreads = kProducerWarp ? 160 : 128;
+};
 constexpr int kMaxPagedChunk = 16384;       // tokens per split at most with a block table
 constexpr int kMergeWarps = 8;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -68,12 +80,10 @@ struct Params {
   int kv_limit;   // local keys that may be read at most
   int batch, q_len, nh, nkv, group;
   int chunk, num_splits;
+  int q_vec16;  // q base and strides allow 16-byte loads
+  int stages;  // ring depth: kMaxStages, or one less when a long block-table slice needs room
   float scale_log2;
 };
-
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
-}
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
@@ -102,14 +112,18 @@ __device__ __forceinline__ void write_partial(const Params& p, int split, int ro
 }
 
 template <int MT, bool PAGED>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* stages = align1024(smem_raw);
-  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kStages * kStageBytes);
-  int* flags = reinterpret_cast<int*>(full + kStages);  // [0] abort
-  int* bt_s = flags + 2;
+  // The ring starts the dynamic shared memory, which must be 1024-aligned for the 128-byte
+  // swizzle; the declaration asks for that and the kernel checks it (no spare room to re-align).
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* stages = smem_raw;
+  const int nst = p.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + nst * kStageBytes);
+  int* flags = reinterpret_cast<int*>(full + kMaxStages);  // [0] abort
+  int* last_fill = flags + 2;                              // tile last issued into each stage
+  int* bt_s = last_fill + kMaxStages;
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
@@ -117,14 +131,30 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  const int pair = warp >> 1;  // warps 0-1 take the even tiles, warps 2-3 the odd ones
+  const int wip = warp & 1;    // 16-token half of the tile this warp takes
+  // Stages are private to a pair: pair g owns stages g, g+2, g+4, ... (ns_pair of them) and its
+  // j-th tile uses stage g + 2 (j % ns_pair). Each stage thus has one consumer, which waits for
+  // its fills in the order they were issued, so a parity wait can never see a fill one phase
+  // early. Tile t < nst lands in stage t.
   const int rows_total = p.batch * p.q_len * p.nh;
   const bool single = p.num_splits == 1;
+  constexpr int kThreads = Shape<MT>::kThreads;
+  const bool consumer = warp < kWarps;
+  const bool initial_issuer = Shape<MT>::kProducerWarp ? (warp == kWarps && lane == 0) : tid == 0;
 
   pdl_launch_dependents();
+  if (smem_u32(smem_raw) & 1023u) {
+    if (tid == 0) atomicOr(&g_decode_status, kDevErrSmemAlign);
+    return;
+  }
   if (tid == 0) {
     prefetch_tensormap(&tmK);
     prefetch_tensormap(&tmV);
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(&full[s], 1);
+      last_fill[s] = -1;
+    }
     flags[0] = 0;
     fence_mbarrier_init();
   }
@@ -176,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int t0 = t_begin + it * kTile;
     const int br = p.box_rows;
     const int nbox = min(kTile, t_end - t0 + br - 1) / br;  // boxes with at least one key
+    last_fill[s] = it;
     mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nbox * br * 128 * 4));
     for (int j = 0; j < nbox; ++j) {
       const int tok = t0 + j * br;
@@ -198,13 +229,59 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   };
 
-  if (tid == 0) {
-    const int n0 = ntiles < kStages ? ntiles : kStages;
+  // Every stage but the last is filled at once; the last one first carries this CTA's query rows.
+  if (initial_issuer) {
+    const int n0 = ntiles < nst - 1 ? ntiles : nst - 1;
     for (int i = 0; i < n0; ++i) issue(i, i);
   }
 
-  // Query fragments (A operand, m16k16 per (mt, ks)); rows past this sequence's rows are zero.
+  // Query fragments (A operand, m16k16 per (mt, ks)). The 37-odd CTAs of a KV head all need the
+  // same rows, so each CTA reads them once with coalesced 16-byte loads into the last stage
+  // (128-byte XOR swizzle, 256 B per row) and builds the fragments with ldmatrix; scattered
+  // per-lane loads of the same few L2 sectors from every CTA take microseconds. Every row of the
+  // q_len tokens is loaded (valid memory); rows past this sequence's q_lens are masked below.
   uint32_t qa[MT][8][4];
+  uint8_t* q_stage = stages + (nst - 1) * kStageBytes;
+  if (consumer) {
+    const int rows_alloc = p.q_len * p.group;
+    for (int idx = tid; idx < MT * 16 * 16; idx += kWarps * 32) {
+      const int r = idx >> 4, c = idx & 15;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < rows_alloc) {
+        const int qi = r / p.group, h = kvh * p.group + r % p.group;
+        const bf16* src = p.q + b * p.q_sb + qi * p.q_st + h * p.q_sh + c * 8;
+        if (p.q_vec16) {
+          v = *reinterpret_cast<const uint4*>(src);
+        } else {
+          const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src);
+          v = make_uint4(s32[0], s32[1], s32[2], s32[3]);
+        }
+      }
+      *reinterpret_cast<uint4*>(q_stage + r * 256 + ((c >> 3) << 7) + (((c & 7) ^ (r & 7)) << 4)) = v;
+    }
+    fence_proxy_async_shared();  // these writes precede the stage's TMA fill
+    asm volatile("bar.sync 3, %0;" ::"n"(kWarps * 32) : "memory");
+    const uint32_t qs = smem_u32(q_stage);
+    const int m = lane >> 3;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int row = mt * 16 + (lane & 7) + (m & 1) * 8;
+        const int kc = 2 * ks + (m >> 1);
+        ldmatrix_x4(qa[mt][ks][0], qa[mt][ks][1], qa[mt][ks][2], qa[mt][ks][3],
+                    qs + row * 256 + ((kc >> 3) << 7) + (((kc & 7) ^ (row & 7)) << 4));
+      }
+    if (Shape<MT>::kProducerWarp)
+      asm volatile("bar.arrive 4, %0;" ::"n"((kWarps + 1) * 32) : "memory");
+    else
+      asm volatile("bar.sync 4, %0;" ::"n"(kWarps * 32) : "memory");
+  } else {
+    __syncwarp();
+    asm volatile("bar.sync 4, %0;" ::"n"((kWarps + 1) * 32) : "memory");
+  }
+  if (initial_issuer && ntiles >= nst) issue(nst - 1, nst - 1);
+
   int lim[MT][2];  // last visible local key of the two rows this lane holds per m-tile
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
@@ -217,20 +294,6 @@ __global__ void __launch_bounds__(kThreads, 2)
         lim[mt][hr] = static_cast<int>(last < -1 ? -1 : last);
       } else {
         lim[mt][hr] = -1;
-      }
-    }
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int r = mt * 16 + (lane >> 2) + (e & 1) * 8;
-        const int c = ks * 16 + (lane & 3) * 2 + (e >> 1) * 8;
-        uint32_t v = 0u;
-        if (r < rows_b) {
-          const int qi = r / p.group, h = kvh * p.group + r % p.group;
-          v = *reinterpret_cast<const uint32_t*>(p.q + b * p.q_sb + qi * p.q_st + h * p.q_sh + c);
-        }
-        qa[mt][ks][e] = v;
       }
     }
   }
@@ -254,15 +317,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   constexpr int kChains = MT == 1 ? 2 : 1;
   const uint32_t stages_u32 = smem_u32(stages);
   bool ok = true;
-  int abort_it = -1;
-  for (int it = 0; it < ntiles; ++it) {
-    const int s = it % kStages;
-    const uint32_t parity = (it / kStages) & 1;
-    if (!mbar_wait(&full[s], parity, &g_decode_status)) {
-      ok = false;
-      flags[0] = 1;
-    }
-    const int tok0 = t_begin + it * kTile + warp * 16;
+  const int ns_pair = (nst + 1 - pair) >> 1;
+  for (int it = consumer ? pair : ntiles, j = 0; it < ntiles; it += 2, ++j) {
+    const int s = pair + 2 * (j % ns_pair);
+    const uint32_t parity = (j / ns_pair) & 1;
+    if (!mbar_wait(&full[s], parity, &g_decode_status)) ok = false;
+    ok = __all_sync(0xffffffffu, ok);  // the mma below needs every lane
+    if (!ok) flags[0] = 1;
+    const int tok0 = t_begin + it * kTile + wip * 16;
     if (ok && tok0 < t_end) {
       const uint32_t Ks = stages_u32 + s * kStageBytes;
       const uint32_t Vs = Ks + kKVBytes;
@@ -272,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         uint8_t* Vg = stages + s * kStageBytes + kKVBytes;
         const int valid = t_end - tok0;
         for (int idx = lane; idx < (16 - valid) * 16; idx += 32) {
-          const int trow = warp * 16 + valid + (idx >> 4);
+          const int trow = wip * 16 + valid + (idx >> 4);
           const int ch = idx & 15;
           *reinterpret_cast<uint4*>(Vg + (ch >> 3) * kHalfBytes + swz128(trow, ch & 7)) =
               make_uint4(0u, 0u, 0u, 0u);
@@ -292,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // S = Q K^T over 128 dims: 8 k-steps, two n8 tiles of tokens.
       {
         const int mi = lane >> 3;
-        const int trow = warp * 16 + ((mi >> 1) << 3) + (lane & 7);
+        const int trow = wip * 16 + ((mi >> 1) << 3) + (lane & 7);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
           const int half = ks >> 2;
@@ -360,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       // O += P V: V^T fragments via ldmatrix.trans, 16 n8 tiles of dims.
       {
         const int mi = lane >> 3;
-        const int trow = warp * 16 + ((mi & 1) << 3) + (lane & 7);
+        const int trow = wip * 16 + ((mi & 1) << 3) + (lane & 7);
 #pragma unroll
         for (int dn = 0; dn < 8; ++dn) {
           const int dchunk = dn * 2 + (mi >> 1);
@@ -375,23 +437,26 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
-    __syncthreads();
-    if (flags[0]) {
-      abort_it = it;
-      break;
-    }
-    if (tid == 0 && it + kStages < ntiles) issue(it + kStages, s);
+    // Both warps of the pair are done with stage s: refill it with the pair's tile ns_pair on.
+    if (pair == 0)
+      asm volatile("bar.sync 1, 64;" ::: "memory");
+    else
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+    if (flags[0]) break;
+    if (wip == 0 && lane == 0 && it + 2 * ns_pair < ntiles) issue(it + 2 * ns_pair, s);
   }
+  __syncthreads();
 
-  if (abort_it >= 0) {
-    // A stage never completed within the time limit. Tiles abort_it .. abort_it+kStages-1 may
-    // still have copies in flight: give each a bounded wait before the CTA releases its shared
-    // memory, and write nothing (the status word tells the host).
+  if (flags[0]) {
+    // A stage never completed within the time limit. The last fill of every stage may still have
+    // copies in flight: give each a bounded wait before the CTA releases its shared memory, and
+    // write nothing (the status word tells the host).
     if (tid == 0) {
-      const int last = min(ntiles, abort_it + kStages);
-      for (int t = abort_it; t < last; ++t) {
-        const uint32_t bar = smem_u32(&full[t % kStages]);
-        const uint32_t par = (t / kStages) & 1;
+      for (int st = 0; st < nst; ++st) {
+        const int t = last_fill[st];
+        if (t < 0) continue;
+        const uint32_t bar = smem_u32(&full[st]);
+        const uint32_t par = (((t >> 1) / ((nst + 1 - (t & 1)) >> 1))) & 1;
         const unsigned long long t0 = globaltimer_ns();
         while (!mbar_try_wait(bar, par) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
@@ -412,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* red = reinterpret_cast<float*>(stages);  // [warps][kRows][kRedStride]
   float* ms = red + kWarps * kRows * kRedStride;   // [warps][kRows]
   float* ls = ms + kWarps * kRows;                 // [warps][kRows]
-  if ((lane & 3) == 0) {
+  if (consumer && (lane & 3) == 0) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -426,7 +491,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int hr = 0; hr < 2; ++hr) {
+    for (int hr = 0; hr < 2 && consumer; ++hr) {
       const int r = mt * 16 + (lane >> 2) + hr * 8;
       float M = -INFINITY;
 #pragma unroll
@@ -572,6 +637,7 @@ struct Plan {
   int kv_limit = 0;
   int chunk = 0;
   int splits = 0;
+  int stages = kMaxStages;
   size_t part_o_bytes = 0;
   size_t part_lse_bytes = 0;
   size_t ws_bytes = 0;
@@ -623,8 +689,12 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl) {
     pl->part_lse_bytes = align_up(static_cast<size_t>(pl->splits) * pl->rows_total * 4, 256);
   }
   pl->ws_bytes = pl->part_o_bytes + pl->part_lse_bytes;
+  // The block-table slice of a split sits after the ring; a long one costs the ring a stage.
   const int bt_ints = pl->paged ? (pl->chunk / a->page_size + 2) : 0;
-  pl->smem_bytes = 1024 + kStages * kStageBytes + kStages * 8 + 8 + bt_ints * 4;
+  const int spare = kSmemPerCta - kMaxStages * kStageBytes - kHdrBytes;
+  pl->stages = bt_ints * 4 <= spare ? kMaxStages : kMaxStages - 1;
+  pl->smem_bytes = static_cast<size_t>(pl->stages) * kStageBytes + kHdrBytes + bt_ints * 4;
+  if (pl->smem_bytes > static_cast<size_t>(kSmemPerCta)) return SOLORT_ERR_UNSUPPORTED;
   return SOLORT_OK;
 }
 
@@ -648,7 +718,7 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& pr
   static unsigned configured = 0;  // one bit per device ordinal < 32
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
-  const size_t max_smem = 1024 + kStages * kStageBytes + 64 + (kMaxPagedChunk / 8 + 2) * 4;
+  const size_t max_smem = kSmemPerCta;
   if (smem > max_smem) return SOLORT_ERR_UNSUPPORTED;
   if (dev >= 32 || !(configured & (1u << dev))) {
     if (cudaFuncSetAttribute(decode_kernel<MT, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -660,7 +730,7 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& pr
     if (dev < 32) configured |= 1u << dev;
   }
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = pdl_config(grid, dim3(kThreads), smem, stream, attr);
+  cudaLaunchConfig_t cfg = pdl_config(grid, dim3(Shape<MT>::kThreads), smem, stream, attr);
   if (cudaLaunchKernelEx(&cfg, decode_kernel<MT, PAGED>, tk, tv, prm) != cudaSuccess)
     return SOLORT_ERR_CUDA;
   return launch_status();
@@ -804,6 +874,8 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
   prm.group = a->num_qo_heads / a->num_kv_heads;
   prm.chunk = pl.chunk;
   prm.num_splits = pl.splits;
+  prm.stages = pl.stages;
+  prm.q_vec16 = aligned(a->q, 16) && ((a->q_stride_batch | a->q_stride_token | a->q_stride_head) & 7) == 0;
   prm.scale_log2 = a->scale * 1.4426950408889634f;
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);

@@ -63,6 +63,40 @@ def test_decode_forced_splits(splits):
     assert_close(out[0], ref, f"splits={splits}")
 
 
+@pytest.mark.parametrize("L,splits", [(65536, 1), (65536, 3), (20000, 5), (8192, 2)])
+def test_decode_long_splits_cycle_the_ring(L, splits):
+    """Splits of thousands of keys refill every shared-memory stage hundreds of times; two calls
+    in a row must agree exactly (no stage is read before its own fill lands)."""
+    ops = _ops()
+    q, k, v = _static_case(L + splits, 32, 8, L, 1)
+    ref, _ = A.attention_fp32(q, k, v, 128**-0.5, L - 1)
+    qpos = torch.tensor([L - 1], dtype=torch.int64, device="cuda")
+    dq, dk, dv = q[None].cuda(), k.cuda(), v.cuda()
+    out = ops.gqa_decode(dq, dk, dv, qpos, num_splits=splits)
+    again = ops.gqa_decode(dq, dk, dv, qpos, num_splits=splits)
+    torch.cuda.synchronize()
+    assert_close(out[0], ref, f"L={L} splits={splits}")
+    assert torch.equal(out, again), "repeat call differs"
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("P", [8, 32])
+def test_paged_long_split_small_pages(P):
+    """One split over 16000 keys: with 8-token pages its block-table slice (2002 entries) does
+    not fit beside the full ring, so the kernel runs with one stage fewer."""
+    ops = _ops()
+    n = 16000
+    q, k, v = A.make_attention_inputs(P + 5, 32, 8, 128, 1, n, n - 1)
+    arena, tables = _paged_setup(P + 6, [(n, k, v)], P, OP.pages_required(n, P) + 3)
+    ref, _ = A.attention_fp32(q, k, v, 128**-0.5, n - 1)
+    bt = torch.tensor([tables[0]], dtype=torch.int32).cuda()
+    qpos = torch.tensor([n - 1], dtype=torch.int64, device="cuda")
+    out = ops.gqa_decode_paged(q[None].cuda(), arena.cuda(), bt, qpos, max_kv_len=n, num_splits=1)
+    torch.cuda.synchronize()
+    assert_close(out[0], ref, f"paged long split P={P}")
+    assert ops.device_status() == 0
+
+
 def test_decode_hnd_layer_buffer():
     """The benchmark's layout: all layers' KV as [layer, 2, nkv, max_len, hd]."""
     ops = _ops()
