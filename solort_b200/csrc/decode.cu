@@ -472,31 +472,50 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) l_run[mt][hr] = warp_sum_quad(l_run[mt][hr]);
 
+  // Latency matters here, not throughput (one short pass per CTA): each warp folds the
+  // cross-warp max and the normaliser into one scale per row before it stores, so the last pass
+  // only adds four vectors.
   constexpr int kRows = MT * 16;
-  constexpr int kRedStride = kHD + 4;  // padded rows: the fragment stores below hit 32 banks
+  constexpr int kRedStride = kHD + 8;  // padded rows: each half-warp's float2 stores hit 32 banks
   float* red = reinterpret_cast<float*>(stages);  // [warps][kRows][kRedStride]
   float* ms = red + kWarps * kRows * kRedStride;   // [warps][kRows]
   float* ls = ms + kWarps * kRows;                 // [warps][kRows]
+  float* lse_s = ls + kWarps * kRows;              // [kRows]
   if (consumer && (lane & 3) == 0) {
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
       for (int hr = 0; hr < 2; ++hr) {
         const int r = mt * 16 + (lane >> 2) + hr * 8;
-        ms[warp * kRows + r] = m_run[mt][hr];
-        ls[warp * kRows + r] = l_run[mt][hr];
+        if (r < rows_b) {
+          ms[warp * kRows + r] = m_run[mt][hr];
+          ls[warp * kRows + r] = l_run[mt][hr];
+        }
       }
   }
   __syncthreads();
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int hr = 0; hr < 2 && consumer; ++hr) {
+    for (int hr = 0; hr < 2; ++hr) {
       const int r = mt * 16 + (lane >> 2) + hr * 8;
+      if (!consumer || r >= rows_b) continue;  // only live rows are combined
+      float mw[kWarps];
       float M = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) M = fmaxf(M, ms[w * kRows + r]);
-      const float f = m_run[mt][hr] == -INFINITY ? 0.f : exp2f(m_run[mt][hr] - M);
+      for (int w = 0; w < kWarps; ++w) {
+        mw[w] = ms[w * kRows + r];
+        M = fmaxf(M, mw[w]);
+      }
+      float L = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w)
+        L += mw[w] == -INFINITY ? 0.f : ls[w * kRows + r] * exp2f(mw[w] - M);
+      // This warp's share of the normalised row: exp2(m_w - M) / L.
+      const float f = (m_run[mt][hr] == -INFINITY || !(L > 0.f))
+                          ? 0.f
+                          : exp2f(m_run[mt][hr] - M) * __frcp_rn(L);
+      if (warp == 0 && (lane & 3) == 0) lse_s[r] = L > 0.f ? (M + __log2f(L)) * kLn2 : -INFINITY;
 #pragma unroll
       for (int n = 0; n < 16; ++n) {
         const int c = n * 8 + (lane & 3) * 2;
@@ -508,28 +527,19 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
 
   for (int idx = tid; idx < rows_b * (kHD / 4); idx += kThreads) {
     const int r = idx / (kHD / 4), c = (idx % (kHD / 4)) * 4;
-    float M = -INFINITY;
+    float4 o = *reinterpret_cast<const float4*>(red + r * kRedStride + c);
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, ms[w * kRows + r]);
-    float L = 0.f;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float mw = ms[w * kRows + r];
-      if (mw != -INFINITY) L += ls[w * kRows + r] * exp2f(mw - M);
+    for (int w = 1; w < kWarps; ++w) {
       const float4 v = *reinterpret_cast<const float4*>(red + (w * kRows + r) * kRedStride + c);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
+      o.x += v.x;
+      o.y += v.y;
+      o.z += v.z;
+      o.w += v.w;
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    const float4 o = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    const float lse = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
     if (single)
-      write_final(p, out_row(r), c, o, lse);
+      write_final(p, out_row(r), c, o, lse_s[r]);
     else
-      write_partial(p, split, rows_total, out_row(r), c, o, lse);
+      write_partial(p, split, rows_total, out_row(r), c, o, lse_s[r]);
   }
 }
 
@@ -622,9 +632,9 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
       o.w += x.w * f;
     }
   }
-  const float inv = D > 0.f ? 1.f / D : 0.f;
+  const float inv = D > 0.f ? __frcp_rn(D) : 0.f;
   write_final(p.out, R, c, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
-              D > 0.f ? M + logf(D) : -INFINITY);
+              D > 0.f ? M + __logf(D) : -INFINITY);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -80,6 +80,55 @@ def test_decode_long_splits_cycle_the_ring(L, splits):
     assert ops.device_status() == 0
 
 
+def test_decode_batch_one_call_ragged_positions():
+    """One call, four sequences over one shared static cache at different positions: splits past a
+    sequence's position hold no key and must merge as empty."""
+    ops = _ops()
+    cap = 4096
+    pos = [5, 4095, 900, 63]
+    q, k, v = A.make_attention_inputs(77, 32, 8, 128, 1, cap, cap - 1)
+    qs = torch.stack([A.make_attention_inputs(80 + i, 32, 8, 128, 1, cap, p)[0]
+                      for i, p in enumerate(pos)])
+    qpos = torch.tensor(pos, dtype=torch.int64, device="cuda")
+    ws = torch.zeros(ops.decode_workspace_bytes(4, 1, 32, 8, cap), dtype=torch.uint8, device="cuda")
+    for rep in range(2):
+        out = ops.gqa_decode(qs.cuda(), k.cuda(), v.cuda(), qpos, workspace=ws)
+        torch.cuda.synchronize()
+        for i, p in enumerate(pos):
+            ref, _ = A.attention_fp32(qs[i], k[: p + 1], v[: p + 1], 128**-0.5, p)
+            assert_close(out[i], ref, f"batch row {i} pos={p} rep={rep}")
+    assert ops.device_status() == 0
+
+
+def test_decode_one_workspace_across_split_plans():
+    """One workspace serves calls with different split plans back to back (a runner's bucket
+    sizes): each call writes every partial it reads."""
+    ops = _ops()
+    cap = 8192
+    q, k, v = A.make_attention_inputs(91, 32, 8, 128, 1, cap, cap - 1)
+    dq, dk, dv = q[None].cuda(), k.cuda(), v.cuda()
+    ws = torch.zeros(ops.decode_workspace_bytes(1, 1, 32, 8, cap), dtype=torch.uint8, device="cuda")
+    for L, splits in ((300, 0), (8192, 0), (8192, 5), (1000, 0), (300, 0), (8192, 0)):
+        qpos = torch.tensor([L - 1], dtype=torch.int64, device="cuda")
+        out = ops.gqa_decode(dq, dk, dv, qpos, max_kv_len=L, workspace=ws, num_splits=splits)
+        torch.cuda.synchronize()
+        ref, _ = A.attention_fp32(q, k[:L], v[:L], 128**-0.5, L - 1)
+        assert_close(out[0], ref, f"L={L} splits={splits}")
+    assert ops.device_status() == 0
+
+
+def test_partial_shard_past_the_query_is_empty():
+    """A shard whose keys all sit after the query position sees nothing: O = 0, LSE = -inf."""
+    ops = _ops()
+    S = 2048
+    q, k, v = A.make_attention_inputs(93, 32, 8, 128, 1, S, S - 1)
+    qpos = torch.tensor([100], dtype=torch.int64, device="cuda")
+    o, lse = ops.gqa_decode_partial(q[None].cuda(), k.cuda(), v.cuda(), qpos, kv_pos_offset=4096)
+    torch.cuda.synchronize()
+    assert (o == 0).all() and torch.isneginf(lse).all()
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("P", [8, 32])
 def test_paged_long_split_small_pages(P):
     """One split over 16000 keys: with 8-token pages its block-table slice (2002 entries) does
@@ -301,7 +350,7 @@ def test_decode_cuda_graph_replay_with_moving_position():
     dq, dk, dv = q[None].cuda(), k.cuda(), v.cuda()
     pos_buf = torch.zeros(1, dtype=torch.int64, device="cuda")
     out = torch.empty_like(dq)
-    ws = torch.empty(ops.decode_workspace_bytes(1, 1, 32, 8, cap), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(ops.decode_workspace_bytes(1, 1, 32, 8, cap), dtype=torch.uint8, device="cuda")
     pos_buf.fill_(100)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
