@@ -46,6 +46,8 @@ def parse_args():
     ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
                     help="decode: BASELINE config 2 (+ prefill section); prefill: config 3 only")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: partials cross GPUs by NVLink peer stores (p2p) or an NCCL all-gather")
     ap.add_argument("--prefill-T", type=int, nargs="+", default=[512, 1024, 4096])
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the paged / long-context / tok/s sections of the default line")
@@ -237,13 +239,15 @@ def run_gpu_arm(args) -> None:
     kv, q, qpos = make_inputs(ctx, rank, world, dev)
     bytes_per_layer = 2 * ctx * NKV * HD * 2  # K + V of this rank's keys
     outs = torch.empty_like(q)
-    ws = torch.empty(max(256, ops.decode_workspace_bytes(1, 1, NH, NKV, ctx)), dtype=torch.uint8,
+    ws = torch.empty(max(256, ops.decode_workspace_bytes(1, 1, NH, NKV, ctx),
+                         ops.decode_exchange_workspace_bytes(1, 1, NH, NKV, ctx)), dtype=torch.uint8,
                      device=dev)
     sharded = None
     if world > 1:
         from solort_b200.sharded import ShardedDecode
 
-        sharded = ShardedDecode(rank, world, num_qo_heads=NH, layers=LAYERS, device=dev)
+        sharded = ShardedDecode(rank, world, num_qo_heads=NH, layers=LAYERS, device=dev,
+                                exchange=args.exchange)
 
     def step():
         for li in range(LAYERS):
@@ -364,6 +368,8 @@ def run_gpu_arm(args) -> None:
             "keys_per_gpu": ctx, "context": ctx * world,
             "kv_layout": "[layer, 2, nkv, max_len, hd] bf16",
             "parallelism": f"seq-shard x{world}" if world > 1 else "single GPU",
+            "exchange": (("NVLink peer stores + flag-synchronised merge" if args.exchange == "p2p"
+                          else "NCCL all_gather_into_tensor + lse_merge") if world > 1 else None),
             "l2": "inputs larger than L2: 36 layers x 32 MiB KV per GPU replayed in order",
             "graph": "36 layer calls per CUDA graph replay",
         },

@@ -4,8 +4,9 @@
  *
  * Every entry point takes raw device pointers, element strides and sizes; no torch types cross
  * this boundary. All kernels are enqueued on the caller's stream (a cudaStream_t passed as
- * `void*`), never allocate, never synchronise the host, and read lengths / positions from device
- * memory, so every call can be captured inside a CUDA graph. Return value: SOLORT_OK (0) or a
+ * `void*`), never allocate (only the set-up calls solort_attn_exchange_buffer_create / _open map
+ * memory), never synchronise the host, and read lengths / positions from device memory, so every
+ * per-step call can be captured inside a CUDA graph. Return value: SOLORT_OK (0) or a
  * negative SOLORT_ERR_* code; no exception crosses the ABI and nothing falls back to another
  * implementation.
  *
@@ -18,7 +19,8 @@
  *   solort_attn_decode with a block table (paged KV, NHD pages [pages, 2, P, nkv, hd]):
  *       src/solort/backends/transformers_flashinfer.py:95-129  (AttentionInterface decode/prefill)
  *       src/solort/cache/kv_cache.py:86-100,136-149            (page layout, slot = bt[p//P]*P+p%P)
- *   solort_attn_decode with out_f32/lse_out + solort_attn_lse_merge:
+ *   solort_attn_decode with out_f32/lse_out + solort_attn_lse_merge, and
+ *   solort_attn_decode_exchange + solort_attn_exchange_merge:
  *       no counterpart (the reference is single-GPU); sequence-sharded long-context decode.
  */
 #ifndef SOLORT_ATTN_H_
@@ -48,6 +50,7 @@ extern "C" {
 #define SOLORT_ERR_TENSOR_MAP (-5)       /* the driver rejected a TMA descriptor */
 #define SOLORT_ERR_NO_DEVICE (-6)        /* no sm_100 device is current */
 #define SOLORT_ERR_SCRATCH_LIMIT (-7)    /* the call needs more split scratch than the static 4 MiB */
+#define SOLORT_ERR_IPC (-8)              /* a CUDA IPC export / import of an exchange buffer failed */
 
 /*
  * GQA attention of q_len query tokens per sequence against a KV cache: decode (q_len == 1),
@@ -159,6 +162,60 @@ typedef struct SolortMergeArgs {
 SOLORT_API int solort_attn_lse_merge(const SolortMergeArgs* args, void* stream);
 
 /*
+ * Sequence-sharded decode with a peer-memory exchange. No counterpart in the reference (it runs on
+ * one GPU); this replaces the all-gather + merge of a partial per rank with direct NVLink stores.
+ *
+ * Each of R ranks (one process per GPU, R <= SOLORT_MAX_RANKS) holds a contiguous shard of the
+ * keys. solort_attn_decode_exchange runs the split-KV decode over the local shard (args as for
+ * solort_attn_decode; out, out_f32, lse_out and q_lens must be NULL) and its merge kernel stores
+ * the rank's partial (O fp32 [rows][128], then natural-log LSE fp32 [rows]; rows =
+ * batch*q_len*num_qo_heads) into slot_in_rank[p] on every rank p -- this rank's slot in p's
+ * receive buffer, a peer pointer for p != rank -- and then sets flag_in_rank[p][row] = 1 with a
+ * system-scope release. solort_attn_exchange_merge, on every rank, waits for all R flags of each
+ * row (one second at most per row; on expiry it sets bit 3 of the device status and leaves the row
+ * unwritten), merges the R partials into bf16 `out` and clears the flags.
+ *
+ * Slots and flags live in buffers from solort_attn_exchange_buffer_create (cudaMalloc'd, zero-filled,
+ * exported as a CUDA IPC handle) and solort_attn_exchange_buffer_open (the peer mapping). A set of
+ * slots and flags may be reused by a later call once every rank has finished the exchange_merge
+ * that read it -- for example one set per layer of a decode step. Workspace: query
+ * solort_attn_decode_exchange_workspace_size() with the same args.
+ */
+#define SOLORT_MAX_RANKS 8
+typedef struct SolortExchangeArgs {
+  int32_t num_ranks;
+  int32_t rank;
+  float* slot_in_rank[SOLORT_MAX_RANKS];     /* [rows*129] fp32 in rank p's memory, 16-aligned */
+  uint32_t* flag_in_rank[SOLORT_MAX_RANKS];  /* [rows] in rank p's memory */
+} SolortExchangeArgs;
+
+SOLORT_API int solort_attn_decode_exchange_workspace_size(const SolortDecodeArgs* args,
+                                                          size_t* bytes);
+SOLORT_API int solort_attn_decode_exchange(const SolortDecodeArgs* args,
+                                           const SolortExchangeArgs* exchange, void* stream);
+
+typedef struct SolortExchangeMergeArgs {
+  const float* slots;  /* rank s's slot at slots + s*slot_stride: [rows*128 O][rows LSE] fp32 */
+  int64_t slot_stride; /* floats between consecutive ranks' slots (>= rows*129, multiple of 4) */
+  uint32_t* flags;     /* rank s's row flags at flags + s*flag_stride */
+  int64_t flag_stride; /* >= rows */
+  int32_t num_ranks;
+  int32_t batch, q_len, num_qo_heads, head_dim;
+  void* out; /* bf16, strided like SolortDecodeArgs.out */
+  int64_t out_stride_batch, out_stride_token, out_stride_head;
+} SolortExchangeMergeArgs;
+
+SOLORT_API int solort_attn_exchange_merge(const SolortExchangeMergeArgs* args, void* stream);
+
+/* Exchange buffers (set-up calls, not for the per-step path): create allocates `bytes` of device
+ * memory on the current device, zero-fills it and writes its 64-byte CUDA IPC handle; open maps a
+ * peer's buffer from its handle; close unmaps an opened buffer; destroy frees a created one. */
+SOLORT_API int solort_attn_exchange_buffer_create(size_t bytes, void** ptr, void* ipc_handle);
+SOLORT_API int solort_attn_exchange_buffer_open(const void* ipc_handle, void** ptr);
+SOLORT_API int solort_attn_exchange_buffer_close(void* ptr);
+SOLORT_API int solort_attn_exchange_buffer_destroy(void* ptr);
+
+/*
  * Causal (or full) GQA prefill on the tcgen05 tensor cores, one sequence.
  *   q   [q_len,  num_qo_heads, 128] bf16, element strides (q_stride_token, q_stride_head)
  *   k,v [kv_len, num_kv_heads, 128] bf16, element strides (kv_stride_token, kv_stride_head)
@@ -187,7 +244,8 @@ SOLORT_API int solort_attn_prefill(const SolortPrefillArgs* args, void* stream);
 /* Reads and clears the device status word of the current device (bit 0: an in-kernel wait hit
  * its time limit and the kernel returned without writing its output; bit 1: a tensor-memory
  * allocation wait hit its limit; bit 2: a kernel found its shared memory misaligned and returned
- * without writing). */
+ * without writing; bit 3: an exchange merge waited a second for a peer's partial and left the
+ * row unwritten). */
 SOLORT_API int solort_attn_device_status(unsigned* flags);
 
 SOLORT_API const char* solort_attn_status_string(int code);

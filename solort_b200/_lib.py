@@ -23,6 +23,7 @@ STATUS_NAMES = {
     -5: "SOLORT_ERR_TENSOR_MAP",
     -6: "SOLORT_ERR_NO_DEVICE",
     -7: "SOLORT_ERR_SCRATCH_LIMIT",
+    -8: "SOLORT_ERR_IPC",
 }
 
 # Every symbol the header declares; tests check the library exports each one.
@@ -35,7 +36,17 @@ EXPORTED_SYMBOLS = (
     "solort_attn_device_status",
     "solort_attn_status_string",
     "solort_attn_abi_version",
+    "solort_attn_decode_exchange_workspace_size",
+    "solort_attn_decode_exchange",
+    "solort_attn_exchange_merge",
+    "solort_attn_exchange_buffer_create",
+    "solort_attn_exchange_buffer_open",
+    "solort_attn_exchange_buffer_close",
+    "solort_attn_exchange_buffer_destroy",
 )
+
+MAX_RANKS = 8  # SOLORT_MAX_RANKS
+IPC_HANDLE_BYTES = 64
 
 c_i32, c_i64, c_f32, c_vp, c_sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
 
@@ -88,6 +99,32 @@ class SolortMergeArgs(ctypes.Structure):
     ]
 
 
+class SolortExchangeArgs(ctypes.Structure):
+    """Mirror of ``SolortExchangeArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("num_ranks", c_i32),
+        ("rank", c_i32),
+        ("slot_in_rank", c_vp * MAX_RANKS),
+        ("flag_in_rank", c_vp * MAX_RANKS),
+    ]
+
+
+class SolortExchangeMergeArgs(ctypes.Structure):
+    """Mirror of ``SolortExchangeMergeArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("slots", c_vp),
+        ("slot_stride", c_i64),
+        ("flags", c_vp),
+        ("flag_stride", c_i64),
+        ("num_ranks", c_i32),
+        ("batch", c_i32), ("q_len", c_i32), ("num_qo_heads", c_i32), ("head_dim", c_i32),
+        ("out", c_vp),
+        ("out_stride_batch", c_i64), ("out_stride_token", c_i64), ("out_stride_head", c_i64),
+    ]
+
+
 _LIB: ctypes.CDLL | None = None
 
 
@@ -126,6 +163,20 @@ def _optional_symbols(lib: ctypes.CDLL) -> None:
     P = ctypes.POINTER
     lib.solort_attn_prefill.argtypes = [P(SolortPrefillArgs), c_vp]
     lib.solort_attn_prefill.restype = ctypes.c_int
+    lib.solort_attn_decode_exchange_workspace_size.argtypes = [P(SolortDecodeArgs), P(c_sz)]
+    lib.solort_attn_decode_exchange_workspace_size.restype = ctypes.c_int
+    lib.solort_attn_decode_exchange.argtypes = [P(SolortDecodeArgs), P(SolortExchangeArgs), c_vp]
+    lib.solort_attn_decode_exchange.restype = ctypes.c_int
+    lib.solort_attn_exchange_merge.argtypes = [P(SolortExchangeMergeArgs), c_vp]
+    lib.solort_attn_exchange_merge.restype = ctypes.c_int
+    lib.solort_attn_exchange_buffer_create.argtypes = [c_sz, P(c_vp), c_vp]
+    lib.solort_attn_exchange_buffer_create.restype = ctypes.c_int
+    lib.solort_attn_exchange_buffer_open.argtypes = [c_vp, P(c_vp)]
+    lib.solort_attn_exchange_buffer_open.restype = ctypes.c_int
+    lib.solort_attn_exchange_buffer_close.argtypes = [c_vp]
+    lib.solort_attn_exchange_buffer_close.restype = ctypes.c_int
+    lib.solort_attn_exchange_buffer_destroy.argtypes = [c_vp]
+    lib.solort_attn_exchange_buffer_destroy.restype = ctypes.c_int
 
 
 class SolortPrefillArgs(ctypes.Structure):

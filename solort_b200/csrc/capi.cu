@@ -4,6 +4,7 @@
 namespace solort {
 int read_decode_status(unsigned* flags);
 int read_prefill_status(unsigned* flags);
+int read_exchange_status(unsigned* flags);
 }  // namespace solort
 
 extern "C" int solort_attn_abi_version(void) { return SOLORT_ATTN_ABI_VERSION; }
@@ -27,6 +28,8 @@ extern "C" const char* solort_attn_status_string(int code) {
     case SOLORT_ERR_SCRATCH_LIMIT:
       return "the call needs more split scratch than the library's static 4 MiB array; use "
              "solort_attn_decode with a workspace";
+    case SOLORT_ERR_IPC:
+      return "CUDA IPC export or import of an exchange buffer failed";
     default:
       return "unknown status";
   }
@@ -39,6 +42,8 @@ extern "C" int solort_attn_device_status(unsigned* flags) {
   int rc = solort::current_device_info(&di);
   if (rc != SOLORT_OK) return rc;
   rc = solort::read_decode_status(flags);
+  if (rc != SOLORT_OK) return rc;
+  rc = solort::read_exchange_status(flags);
   if (rc != SOLORT_OK) return rc;
   return solort::read_prefill_status(flags);
 }

@@ -81,6 +81,7 @@ struct Params {
   int batch, q_len, nh, nkv, group;
   int chunk, num_splits;
   int q_vec16;  // q base and strides allow 16-byte loads
+  int force_partial;  // one split still goes through the partials and the merge kernel
   int stages;  // ring depth: kMaxStages, or one less when a long block-table slice needs room
   float scale_log2;
 };
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
   // its fills in the order they were issued, so a parity wait can never see a fill one phase
   // early. Tile t < nst lands in stage t.
   const int rows_total = p.batch * p.q_len * p.nh;
-  const bool single = p.num_splits == 1;
+  const bool single = p.num_splits == 1 && !p.force_partial;
   constexpr int kThreads = Shape<MT>::kThreads;
   const bool consumer = warp < kWarps;
   const bool initial_issuer = Shape<MT>::kProducerWarp ? (warp == kWarps && lane == 0) : tid == 0;
@@ -552,6 +553,11 @@ struct MergeParams {
   int rows_total;
   const int32_t* q_lens;  // optional: rows whose token index is past q_lens[b] are skipped
   Params out;             // output fields only (out / out_f32 / lse_out, strides, q_len, nh)
+  // Exchange mode (n_dest > 0): instead of `out`, each row goes to n_dest packed slots
+  // [rows*128 O][rows LSE] (peer memory for all but this rank), then its flag in each is set.
+  int n_dest;
+  float* dest[SOLORT_MAX_RANKS];
+  unsigned* dest_flag[SOLORT_MAX_RANKS];
 };
 
 // One CTA per output row, 8 warps; warp g takes parts g, g+8, ... and lane l dims 4l..4l+3.
@@ -633,8 +639,23 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
     }
   }
   const float inv = D > 0.f ? __frcp_rn(D) : 0.f;
-  write_final(p.out, R, c, make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv),
-              D > 0.f ? M + __logf(D) : -INFINITY);
+  const float4 res = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+  const float lse = D > 0.f ? M + __logf(D) : -INFINITY;
+  if (p.n_dest == 0) {
+    write_final(p.out, R, c, res, lse);
+    return;
+  }
+  // Exchange: store the row into every rank's slot (NVLink stores for peers), make the stores
+  // visible system-wide, then raise the row's flag in each slot with a release store.
+  for (int d = 0; d < p.n_dest; ++d) {
+    *reinterpret_cast<float4*>(p.dest[d] + static_cast<int64_t>(R) * kHD + c) = res;
+    if (lane == 0) p.dest[d][static_cast<int64_t>(p.rows_total) * kHD + R] = lse;
+  }
+  __threadfence_system();
+  __syncwarp();
+  if (lane < p.n_dest)
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.dest_flag[lane] + R), "r"(1u)
+                 : "memory");
 }
 
 // ------------------------------------------------------------------------------------------
@@ -648,6 +669,7 @@ struct Plan {
   int chunk = 0;
   int splits = 0;
   int stages = kMaxStages;
+  bool force_partial = false;  // exchange calls always merge through the partials
   size_t part_o_bytes = 0;
   size_t part_lse_bytes = 0;
   size_t ws_bytes = 0;
@@ -657,7 +679,7 @@ struct Plan {
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-int make_plan(const SolortDecodeArgs* a, Plan* pl) {
+int make_plan(const SolortDecodeArgs* a, Plan* pl, bool force_partial = false) {
   if (!a || !pl) return SOLORT_ERR_INVALID_ARGUMENT;
   if (a->head_dim != kHD) return SOLORT_ERR_UNSUPPORTED;
   if (a->batch <= 0 || a->q_len <= 0 || a->num_qo_heads <= 0 || a->num_kv_heads <= 0)
@@ -694,7 +716,8 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl) {
   if (splits > (1ll << 31) - 1) return SOLORT_ERR_UNSUPPORTED;
   pl->splits = static_cast<int>(splits);
   pl->rows_total = a->batch * a->q_len * a->num_qo_heads;
-  if (pl->splits > 1) {
+  pl->force_partial = force_partial;
+  if (pl->splits > 1 || force_partial) {
     pl->part_o_bytes = align_up(static_cast<size_t>(pl->splits) * pl->rows_total * kHD * 4, 256);
     pl->part_lse_bytes = align_up(static_cast<size_t>(pl->splits) * pl->rows_total * 4, 256);
   }
@@ -831,19 +854,34 @@ extern "C" int solort_attn_decode_workspace_size(const SolortDecodeArgs* a, size
   return SOLORT_OK;
 }
 
-extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
+namespace solort {
+namespace dec {
+
+// Shared by solort_attn_decode and solort_attn_decode_exchange (x != nullptr: the merge kernel
+// sends every row to the ranks' slots instead of writing an output).
+int decode_impl(const SolortDecodeArgs* a, const SolortExchangeArgs* x, void* stream_v) {
   Plan pl;
-  int rc = make_plan(a, &pl);
+  int rc = make_plan(a, &pl, x != nullptr);
   if (rc != SOLORT_OK) return rc;
   if (!a->q || !a->k || !a->v || !a->q_pos) return SOLORT_ERR_INVALID_ARGUMENT;
   const bool partial_out = a->lse_out != nullptr;
-  if (partial_out ? !a->out_f32 : !a->out) return SOLORT_ERR_INVALID_ARGUMENT;
+  if (x) {
+    if (a->out || a->out_f32 || a->lse_out || a->q_lens) return SOLORT_ERR_INVALID_ARGUMENT;
+    if (x->num_ranks < 1 || x->num_ranks > SOLORT_MAX_RANKS || x->rank < 0 ||
+        x->rank >= x->num_ranks)
+      return SOLORT_ERR_INVALID_ARGUMENT;
+    for (int d = 0; d < x->num_ranks; ++d)
+      if (!aligned(x->slot_in_rank[d], 16) || !aligned(x->flag_in_rank[d], 4))
+        return SOLORT_ERR_INVALID_ARGUMENT;
+  } else if (partial_out ? !a->out_f32 : !a->out) {
+    return SOLORT_ERR_INVALID_ARGUMENT;
+  }
   if (!aligned(a->q, 4) || (a->q_stride_batch | a->q_stride_token | a->q_stride_head) & 1)
     return SOLORT_ERR_INVALID_ARGUMENT;
-  if (!partial_out &&
+  if (!x && !partial_out &&
       (!aligned(a->out, 8) || (a->out_stride_batch | a->out_stride_token | a->out_stride_head) & 3))
     return SOLORT_ERR_INVALID_ARGUMENT;
-  if (partial_out && (!aligned(a->out_f32, 16) || !aligned(a->lse_out, 4)))
+  if (!x && partial_out && (!aligned(a->out_f32, 16) || !aligned(a->lse_out, 4)))
     return SOLORT_ERR_INVALID_ARGUMENT;
   if (pl.paged && (!a->block_table || a->block_table_stride <= 0)) return SOLORT_ERR_INVALID_ARGUMENT;
   if (pl.ws_bytes > 0 &&
@@ -861,7 +899,7 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
   prm.q_st = a->q_stride_token;
   prm.q_sh = a->q_stride_head;
   fill_output_fields(a, &prm);
-  if (pl.splits > 1) {
+  if (pl.splits > 1 || pl.force_partial) {
     uint8_t* ws = static_cast<uint8_t*>(a->workspace);
     prm.part_o = reinterpret_cast<float*>(ws);
     prm.part_lse = reinterpret_cast<float*>(ws + pl.part_o_bytes);
@@ -885,6 +923,7 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
   prm.chunk = pl.chunk;
   prm.num_splits = pl.splits;
   prm.stages = pl.stages;
+  prm.force_partial = pl.force_partial ? 1 : 0;
   prm.q_vec16 = aligned(a->q, 16) && ((a->q_stride_batch | a->q_stride_token | a->q_stride_head) & 7) == 0;
   prm.scale_log2 = a->scale * 1.4426950408889634f;
 
@@ -897,7 +936,7 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
     rc = pl.paged ? launch_decode<2, true>(tk, tv, prm, grid, pl.smem_bytes, stream)
                   : launch_decode<2, false>(tk, tv, prm, grid, pl.smem_bytes, stream);
   }
-  if (rc != SOLORT_OK || pl.splits == 1) return rc;
+  if (rc != SOLORT_OK || (pl.splits == 1 && !pl.force_partial)) return rc;
   MergeParams mp{};
   mp.o_parts = prm.part_o;
   mp.part_stride = static_cast<int64_t>(pl.rows_total) * kHD;
@@ -907,7 +946,37 @@ extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream_v) {
   mp.rows_total = pl.rows_total;
   mp.q_lens = a->q_lens;
   fill_output_fields(a, &mp.out);
+  if (x) {
+    mp.n_dest = x->num_ranks;
+    for (int d = 0; d < x->num_ranks; ++d) {
+      mp.dest[d] = x->slot_in_rank[d];
+      mp.dest_flag[d] = x->flag_in_rank[d];
+    }
+  }
   return launch_merge(mp, stream);
+}
+
+}  // namespace dec
+}  // namespace solort
+
+extern "C" int solort_attn_decode(const SolortDecodeArgs* a, void* stream) {
+  return decode_impl(a, nullptr, stream);
+}
+
+extern "C" int solort_attn_decode_exchange_workspace_size(const SolortDecodeArgs* a,
+                                                          size_t* bytes) {
+  if (!bytes) return SOLORT_ERR_INVALID_ARGUMENT;
+  Plan pl;
+  int rc = make_plan(a, &pl, true);
+  if (rc != SOLORT_OK) return rc;
+  *bytes = pl.ws_bytes;
+  return SOLORT_OK;
+}
+
+extern "C" int solort_attn_decode_exchange(const SolortDecodeArgs* a, const SolortExchangeArgs* x,
+                                           void* stream) {
+  if (!a || !x) return SOLORT_ERR_INVALID_ARGUMENT;
+  return decode_impl(a, x, stream);
 }
 
 extern "C" int solort_attn_lse_merge(const SolortMergeArgs* a, void* stream_v) {

@@ -333,6 +333,76 @@ def lse_merge(
     return res
 
 
+def decode_exchange_workspace_bytes(
+    batch: int, q_len: int, num_qo_heads: int, num_kv_heads: int, max_kv_len: int,
+    *, kv_capacity: int | None = None, num_splits: int = 0,
+) -> int:
+    """Workspace bytes a ``gqa_decode_exchange`` call with these sizes needs on the current device."""
+    a = _lib.SolortDecodeArgs()
+    a.batch, a.q_len, a.num_qo_heads, a.num_kv_heads, a.head_dim = (
+        batch, q_len, num_qo_heads, num_kv_heads, HEAD_DIM)
+    a.max_kv_len = max_kv_len
+    a.kv_capacity = kv_capacity if kv_capacity is not None else max_kv_len
+    a.num_splits = num_splits
+    need = ctypes.c_size_t(0)
+    _lib.check(_lib.load().solort_attn_decode_exchange_workspace_size(ctypes.byref(a), ctypes.byref(need)),
+               "solort_attn_decode_exchange_workspace_size")
+    return int(need.value)
+
+
+def gqa_decode_exchange(
+    q: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    q_pos: torch.Tensor,
+    exchange: _lib.SolortExchangeArgs,
+    *,
+    kv_pos_offset: int = 0,
+    kv_layout: str = "NHD",
+    scale: float | None = None,
+    max_kv_len: int | None = None,
+    workspace: torch.Tensor | None = None,
+    num_splits: int = 0,
+) -> None:
+    """Decode over this rank's key shard and store the rank's partial ``(O, LSE)`` into its slot
+    on every rank named by ``exchange`` (peer-memory stores), raising the rows' flags there."""
+    cap, nkv, st, sh = _static_kv(k_cache, v_cache, kv_layout)
+    a = _decode_args(
+        q, k_cache, v_cache, q_pos, stride_token=st, stride_head=sh, stride_page=0,
+        kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
+        scale=scale, max_kv_len=max_kv_len or cap, out=None, out_f32=None, lse_out=None,
+        q_lens=None, kv_pos_offset=kv_pos_offset, num_splits=num_splits)
+    lib = _lib.load()
+    need = ctypes.c_size_t(0)
+    _lib.check(lib.solort_attn_decode_exchange_workspace_size(ctypes.byref(a), ctypes.byref(need)),
+               "solort_attn_decode_exchange_workspace_size")
+    if workspace is None:
+        workspace = torch.empty(need.value, dtype=torch.uint8, device=q.device)
+    a.workspace = workspace.data_ptr()
+    a.workspace_bytes = workspace.numel() * workspace.element_size()
+    _lib.check(lib.solort_attn_decode_exchange(ctypes.byref(a), ctypes.byref(exchange),
+                                               ctypes.c_void_p(_stream(q.device))),
+               "solort_attn_decode_exchange")
+
+
+def exchange_merge(slots: int, slot_stride: int, flags: int, flag_stride: int, num_ranks: int,
+                   out: torch.Tensor) -> torch.Tensor:
+    """Wait for every rank's partial in this rank's receive slots / flags (device addresses; rank
+    ``s`` at ``slots + s * slot_stride`` floats and ``flags + s * flag_stride`` words), merge them
+    into bf16 ``out [B, q_len, nh, 128]`` and clear the flags."""
+    _check_cuda("out", out, torch.bfloat16)
+    B, T, H, D = out.shape
+    m = _lib.SolortExchangeMergeArgs()
+    m.slots, m.slot_stride, m.flags, m.flag_stride = slots, slot_stride, flags, flag_stride
+    m.num_ranks = num_ranks
+    m.batch, m.q_len, m.num_qo_heads, m.head_dim = B, T, H, D
+    m.out = out.data_ptr()
+    m.out_stride_batch, m.out_stride_token, m.out_stride_head = out.stride(0), out.stride(1), out.stride(2)
+    _lib.check(_lib.load().solort_attn_exchange_merge(ctypes.byref(m), ctypes.c_void_p(_stream(out.device))),
+               "solort_attn_exchange_merge")
+    return out
+
+
 def device_status() -> int:
     """Read and clear the library's device status word (nonzero: an in-kernel wait timed out)."""
     flags = ctypes.c_uint(0)

@@ -1,45 +1,177 @@
 """Sequence-sharded long-context decode across GPUs (one process per GPU).
 
 The reference is single-GPU; this is the engine's one sharded path. Rank ``r`` of ``R`` holds the
-keys ``[r * S, (r + 1) * S)`` of the sequence in its own HBM. Per layer:
+keys ``[r * S, (r + 1) * S)`` of the sequence in its own HBM; local key ``t`` sits at position
+``r * S + t`` (``kv_pos_offset``), so causal limits stay exact at shard boundaries. Per layer each
+rank computes its partial ``O`` (fp32 ``[rows, 128]``) and natural-log ``LSE`` (``[rows]``), the
+partials reach every rank, and each rank merges the ``R`` of them into the bf16 output.
 
-1. ``gqa_decode_partial`` over the local shard (split-KV decode + merge of its own splits) writes
-   the rank's partial ``O`` (fp32, ``[rows, 128]``) and natural-log ``LSE`` (``[rows]``) into one
-   packed buffer ``[rows * 129]``; local key ``t`` sits at position ``r * S + t``
-   (``kv_pos_offset``), so causal limits stay exact at shard boundaries.
-2. ``torch.distributed.all_gather_into_tensor`` (NCCL over NVLink / NVSwitch) brings every
-   rank's packed partial into this GPU's memory: ``R * rows * 129 * 4`` bytes (16.5 KB per rank
-   for 32 heads). No kernel reads peer memory, and every TMA load targets only its own CTA.
-3. ``lse_merge`` combines the ``R`` partials into the bf16 output on every rank.
+Two exchanges:
 
-All buffers are allocated at construction, one set per layer, so a whole decode step (with its
-NCCL calls) can be captured in one CUDA graph. The partial / merge functions are injectable so
-the rank logic can also run on CPU ranks (``gloo``) against the oracle in tests.
+* ``exchange="p2p"`` (the GPU path ``bench.py`` runs): ``gqa_decode_exchange`` -- the split-KV decode whose merge
+  kernel stores the rank's partial rows straight into its slot on every rank over NVLink and raises
+  a flag per row there -- then ``exchange_merge``, which waits (bounded) for the flags, merges and
+  clears them. The slots live in ``PeerExchange`` buffers: plain allocations exported by CUDA IPC
+  and mapped point to point by every peer. No collective library and no load from peer memory.
+* ``exchange="nccl"``: ``gqa_decode_partial`` into a packed ``[rows * 129]`` buffer,
+  ``torch.distributed.all_gather_into_tensor`` (NCCL over NVLink / NVSwitch), then ``lse_merge``.
+  The partial / merge functions are injectable so this rank logic also runs on CPU ranks
+  (``gloo``) against the oracle in tests.
+
+Everything is allocated at construction, one slot set per layer, so a whole decode step can be
+captured in one CUDA graph: a layer's slots are written again only in the next step, after every
+rank has finished reading them (each rank's next-step send for that layer follows, in stream order,
+its receipt of the other ranks' partials for all later layers of this step).
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 
 HEAD_DIM = 128
+SLOT_FLOATS_PER_ROW = HEAD_DIM + 1  # O row + its LSE
+
+
+def exchange_layout(rank: int, world: int, rows: int, layers: int) -> dict:
+    """Byte layout of one rank's exchange buffer: ``[layers][world]`` slots of ``rows * 129`` fp32
+    (padded to 256 bytes, so every slot is 16-byte aligned), then ``[layers][world][rows]`` uint32
+    flags. Slot ``(li, src)`` receives rank ``src``'s partial for layer ``li``. Returns the sizes
+    and two offset functions."""
+    slot_bytes = -(-rows * SLOT_FLOATS_PER_ROW * 4 // 256) * 256
+    data_bytes = -(-layers * world * slot_bytes // 256) * 256
+    flag_bytes = layers * world * rows * 4
+
+    def slot(li: int, src: int) -> int:
+        return (li * world + src) * slot_bytes
+
+    def flags(li: int, src: int) -> int:
+        return data_bytes + (li * world + src) * rows * 4
+
+    return {"slot_bytes": slot_bytes, "data_bytes": data_bytes, "flag_bytes": flag_bytes,
+            "total_bytes": data_bytes + flag_bytes, "slot": slot, "flags": flags}
+
+
+class PeerExchange:
+    """This rank's receive buffer plus the mappings of every peer's, for ``layers`` slot sets."""
+
+    def __init__(self, rank: int, world: int, rows: int, layers: int, group=None, *,
+                 emulated_bases: list[int] | None = None):
+        from solort_b200 import _lib
+
+        if not 1 <= world <= _lib.MAX_RANKS:
+            raise RuntimeError(f"the peer exchange supports 1..{_lib.MAX_RANKS} ranks, got {world}")
+        self.lib = _lib.load()
+        self.rank, self.world, self.rows, self.layers, self.group = rank, world, rows, layers, group
+        self.layout = exchange_layout(rank, world, rows, layers)
+        if emulated_bases is not None:
+            # All ranks in this process on one GPU (see emulate()): nothing to map.
+            self.base, self.own = list(emulated_bases), emulated_bases[rank]
+            self.opened, self.owns_buffer = [], False
+            self.send_args = [self._send_args(li) for li in range(layers)]
+            return
+        self.owns_buffer = True
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+        _lib.check(self.lib.solort_attn_exchange_buffer_create(self.layout["total_bytes"],
+                                                               ctypes.byref(ptr), handle),
+                   "solort_attn_exchange_buffer_create")
+        self.own = ptr.value
+        handles = [bytes(handle)]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        self.base = [0] * world
+        self.opened = []
+        for p in range(world):
+            if p == rank:
+                self.base[p] = self.own
+                continue
+            peer = ctypes.c_void_p()
+            hb = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES).from_buffer_copy(handles[p])
+            _lib.check(self.lib.solort_attn_exchange_buffer_open(hb, ctypes.byref(peer)),
+                       "solort_attn_exchange_buffer_open")
+            self.base[p] = peer.value
+            self.opened.append(peer.value)
+        if world > 1:
+            dist.barrier(group=group)  # every buffer is mapped everywhere before anyone writes
+        self.send_args = [self._send_args(li) for li in range(layers)]
+
+    def _send_args(self, li: int):
+        from solort_b200 import _lib
+
+        x = _lib.SolortExchangeArgs()
+        x.num_ranks, x.rank = self.world, self.rank
+        for p in range(self.world):
+            x.slot_in_rank[p] = self.base[p] + self.layout["slot"](li, self.rank)
+            x.flag_in_rank[p] = self.base[p] + self.layout["flags"](li, self.rank)
+        return x
+
+    def recv(self, li: int) -> tuple[int, int, int, int]:
+        """This rank's receive slots and flags for layer ``li``: (slot address, slot stride in
+        floats, flag address, flag stride in words), rank ``s`` at ``+ s * stride``."""
+        lay = self.layout
+        return (self.own + lay["slot"](li, 0), lay["slot_bytes"] // 4,
+                self.own + lay["flags"](li, 0), self.rows)
+
+    @classmethod
+    def emulate(cls, world: int, rows: int, layers: int) -> list["PeerExchange"]:
+        """``world`` ranks' exchanges inside this process on the current GPU, for tests: every
+        rank's buffer is local memory, and a caller that runs all ranks' sends before any rank's
+        merge never has a kernel waiting on one that has not finished."""
+        from solort_b200 import _lib
+
+        lib = _lib.load()
+        lay = exchange_layout(0, world, rows, layers)
+        bases = []
+        for _ in range(world):
+            ptr = ctypes.c_void_p()
+            handle = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+            _lib.check(lib.solort_attn_exchange_buffer_create(lay["total_bytes"], ctypes.byref(ptr),
+                                                              handle),
+                       "solort_attn_exchange_buffer_create")
+            bases.append(ptr.value)
+        xs = [cls(r, world, rows, layers, emulated_bases=bases) for r in range(world)]
+        for x in xs:
+            x.owns_buffer = True  # each emulated rank frees its own buffer on close()
+        return xs
+
+    def close(self) -> None:
+        if self.own is None:
+            return
+        if self.opened:
+            dist.barrier(group=self.group)  # nobody stores into a buffer that is going away
+        for p in self.opened:
+            self.lib.solort_attn_exchange_buffer_close(ctypes.c_void_p(p))
+        if self.owns_buffer:
+            self.lib.solort_attn_exchange_buffer_destroy(ctypes.c_void_p(self.own))
+        self.own, self.opened = None, []
 
 
 class ShardedDecode:
     def __init__(self, rank: int, world: int, *, num_qo_heads: int, layers: int,
                  device: torch.device, batch: int = 1, q_len: int = 1, group=None,
-                 partial_fn=None, merge_fn=None, kv_layout: str = "HND"):
+                 partial_fn=None, merge_fn=None, kv_layout: str = "HND", exchange: str = "nccl"):
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(exchange)
+        self.rank, self.world, self.group = rank, world, group
+        self.exchange = exchange
+        self.kv_layout = kv_layout
+        self.shape = (batch, q_len, num_qo_heads)
+        self.rows = batch * q_len * num_qo_heads
+        self.width = self.rows * (HEAD_DIM + 1)
+        self.px = None
+        if exchange == "p2p":
+            self.px = PeerExchange(rank, world, self.rows, layers, group=group)
+            return
         if partial_fn is None or merge_fn is None:
             from solort_b200 import ops
 
             partial_fn = partial_fn or ops.gqa_decode_partial
             merge_fn = merge_fn or ops.lse_merge
-        self.rank, self.world, self.group = rank, world, group
         self.partial_fn, self.merge_fn = partial_fn, merge_fn
-        self.kv_layout = kv_layout
-        self.shape = (batch, q_len, num_qo_heads)
-        self.rows = batch * q_len * num_qo_heads
-        self.width = self.rows * (HEAD_DIM + 1)
         self.send = torch.empty(layers, self.width, dtype=torch.float32, device=device)
         self.recv = torch.empty(layers, world * self.width, dtype=torch.float32, device=device)
 
@@ -58,6 +190,13 @@ class ShardedDecode:
               workspace: torch.Tensor | None = None) -> torch.Tensor:
         """Attention of ``q [B, q_len, nh, 128]`` over the whole sharded sequence of layer ``li``;
         ``k_shard``/``v_shard`` are this rank's keys, first one at ``kv_pos_offset``."""
+        if self.px is not None:
+            from solort_b200 import ops
+
+            ops.gqa_decode_exchange(q, k_shard, v_shard, q_pos, self.px.send_args[li],
+                                    kv_pos_offset=kv_pos_offset, kv_layout=self.kv_layout,
+                                    workspace=workspace)
+            return ops.exchange_merge(*self.px.recv(li), self.world, out)
         buf, o, lse, o_parts, lse_parts = self._views(li)
         self.partial_fn(q, k_shard, v_shard, q_pos, kv_pos_offset=kv_pos_offset,
                         kv_layout=self.kv_layout, out_f32=o, lse_out=lse, workspace=workspace)
@@ -68,4 +207,7 @@ class ShardedDecode:
         return self.merge_fn(o_parts, lse_parts, out=out)
 
     def close(self) -> None:
+        if self.px is not None:
+            self.px.close()
+            self.px = None
         self.send = self.recv = None

@@ -65,7 +65,9 @@ def _c_layout(struct: str, fields: list[str]) -> dict[str, int]:
     return {ln.split()[0]: int(ln.split()[1]) for ln in out.splitlines()}
 
 
-STRUCTS = [(_lib.SolortDecodeArgs, "SolortDecodeArgs"), (_lib.SolortMergeArgs, "SolortMergeArgs")]
+STRUCTS = [(_lib.SolortDecodeArgs, "SolortDecodeArgs"), (_lib.SolortMergeArgs, "SolortMergeArgs"),
+           (_lib.SolortExchangeArgs, "SolortExchangeArgs"),
+           (_lib.SolortExchangeMergeArgs, "SolortExchangeMergeArgs")]
 
 
 @pytest.mark.parametrize("cls,name", STRUCTS + ([(_lib.SolortPrefillArgs, "SolortPrefillArgs")]
