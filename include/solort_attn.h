@@ -168,25 +168,26 @@ SOLORT_API int solort_attn_lse_merge(const SolortMergeArgs* args, void* stream);
  * Each of R ranks (one process per GPU, R <= SOLORT_MAX_RANKS) holds a contiguous shard of the
  * keys. solort_attn_decode_exchange runs the split-KV decode over the local shard (args as for
  * solort_attn_decode; out, out_f32, lse_out and q_lens must be NULL) and its merge kernel stores
- * the rank's partial (O fp32 [rows][128], then natural-log LSE fp32 [rows]; rows =
- * batch*q_len*num_qo_heads) into slot_in_rank[p] on every rank p -- this rank's slot in p's
- * receive buffer, a peer pointer for p != rank -- and then sets flag_in_rank[p][row] = 1 with a
- * system-scope release. solort_attn_exchange_merge, on every rank, waits for all R flags of each
- * row (one second at most per row; on expiry it sets bit 3 of the device status and leaves the row
- * unwritten), merges the R partials into bf16 `out` and clears the flags.
+ * the rank's partial into slot_in_rank[p] on every rank p -- this rank's slot in p's receive
+ * buffer, a peer pointer for p != rank. A slot is rows*129 64-bit words (rows =
+ * batch*q_len*num_qo_heads): word r*128+d holds O[r][d], word rows*128+r the natural-log LSE of
+ * row r, each as (1 << 32) | float bits, written with one 64-bit store, so every word carries its
+ * own arrival mark and no fence or flag is needed. solort_attn_exchange_merge, on every rank,
+ * waits until all R slots of each row are marked (one second at most per row; on expiry it sets
+ * bit 3 of the device status and leaves the row unwritten), merges the R partials into bf16
+ * `out` and zeroes the words it read, ready for the next use of the slots.
  *
- * Slots and flags live in buffers from solort_attn_exchange_buffer_create (cudaMalloc'd, zero-filled,
+ * Slots live in buffers from solort_attn_exchange_buffer_create (cudaMalloc'd, zero-filled,
  * exported as a CUDA IPC handle) and solort_attn_exchange_buffer_open (the peer mapping). A set of
- * slots and flags may be reused by a later call once every rank has finished the exchange_merge
- * that read it -- for example one set per layer of a decode step. Workspace: query
+ * slots may be reused by a later call once every rank has finished the exchange_merge that read
+ * it -- for example one set per layer of a decode step. Workspace: query
  * solort_attn_decode_exchange_workspace_size() with the same args.
  */
 #define SOLORT_MAX_RANKS 8
 typedef struct SolortExchangeArgs {
   int32_t num_ranks;
   int32_t rank;
-  float* slot_in_rank[SOLORT_MAX_RANKS];     /* [rows*129] fp32 in rank p's memory, 16-aligned */
-  uint32_t* flag_in_rank[SOLORT_MAX_RANKS];  /* [rows] in rank p's memory */
+  uint64_t* slot_in_rank[SOLORT_MAX_RANKS]; /* rows*129 words in rank p's memory, 16-aligned */
 } SolortExchangeArgs;
 
 SOLORT_API int solort_attn_decode_exchange_workspace_size(const SolortDecodeArgs* args,
@@ -195,10 +196,8 @@ SOLORT_API int solort_attn_decode_exchange(const SolortDecodeArgs* args,
                                            const SolortExchangeArgs* exchange, void* stream);
 
 typedef struct SolortExchangeMergeArgs {
-  const float* slots;  /* rank s's slot at slots + s*slot_stride: [rows*128 O][rows LSE] fp32 */
-  int64_t slot_stride; /* floats between consecutive ranks' slots (>= rows*129, multiple of 4) */
-  uint32_t* flags;     /* rank s's row flags at flags + s*flag_stride */
-  int64_t flag_stride; /* >= rows */
+  uint64_t* slots;     /* rank s's slot (rows*129 words) at slots + s*slot_stride */
+  int64_t slot_stride; /* words between consecutive ranks' slots (>= rows*129, even) */
   int32_t num_ranks;
   int32_t batch, q_len, num_qo_heads, head_dim;
   void* out; /* bf16, strided like SolortDecodeArgs.out */

@@ -106,7 +106,6 @@ class SolortExchangeArgs(ctypes.Structure):
         ("num_ranks", c_i32),
         ("rank", c_i32),
         ("slot_in_rank", c_vp * MAX_RANKS),
-        ("flag_in_rank", c_vp * MAX_RANKS),
     ]
 
 
@@ -116,8 +115,6 @@ class SolortExchangeMergeArgs(ctypes.Structure):
     _fields_ = [
         ("slots", c_vp),
         ("slot_stride", c_i64),
-        ("flags", c_vp),
-        ("flag_stride", c_i64),
         ("num_ranks", c_i32),
         ("batch", c_i32), ("q_len", c_i32), ("num_qo_heads", c_i32), ("head_dim", c_i32),
         ("out", c_vp),

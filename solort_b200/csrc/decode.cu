@@ -553,12 +553,18 @@ struct MergeParams {
   int rows_total;
   const int32_t* q_lens;  // optional: rows whose token index is past q_lens[b] are skipped
   Params out;             // output fields only (out / out_f32 / lse_out, strides, q_len, nh)
-  // Exchange mode (n_dest > 0): instead of `out`, each row goes to n_dest packed slots
-  // [rows*128 O][rows LSE] (peer memory for all but this rank), then its flag in each is set.
+  // Exchange mode (n_dest > 0): instead of `out`, each row goes to n_dest slots of tagged 64-bit
+  // words [rows*128 O][rows LSE] (peer memory for all but this rank).
   int n_dest;
-  float* dest[SOLORT_MAX_RANKS];
-  unsigned* dest_flag[SOLORT_MAX_RANKS];
+  unsigned long long* dest[SOLORT_MAX_RANKS];
 };
+
+// One exchange word: the arrival mark in the high half, the float's bits in the low half, written
+// by a single 64-bit store (single-copy atomic), so a reader that sees the mark sees the value.
+__device__ __forceinline__ void store_tagged(unsigned long long* w, float v) {
+  const unsigned long long x = (1ull << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(w), "l"(x) : "memory");
+}
 
 // One CTA per output row, 8 warps; warp g takes parts g, g+8, ... and lane l dims 4l..4l+3.
 // Every thread issues all of its loads before using any, so a row costs one round trip.
@@ -645,17 +651,16 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
     write_final(p.out, R, c, res, lse);
     return;
   }
-  // Exchange: store the row into every rank's slot (NVLink stores for peers), make the stores
-  // visible system-wide, then raise the row's flag in each slot with a release store.
+  // Exchange: the row goes into every rank's slot as tagged words (NVLink stores for peers); the
+  // marks make the words self-announcing, so no fence or flag follows.
   for (int d = 0; d < p.n_dest; ++d) {
-    *reinterpret_cast<float4*>(p.dest[d] + static_cast<int64_t>(R) * kHD + c) = res;
-    if (lane == 0) p.dest[d][static_cast<int64_t>(p.rows_total) * kHD + R] = lse;
+    unsigned long long* w = p.dest[d] + static_cast<int64_t>(R) * kHD + c;
+    store_tagged(w + 0, res.x);
+    store_tagged(w + 1, res.y);
+    store_tagged(w + 2, res.z);
+    store_tagged(w + 3, res.w);
+    if (lane == 0) store_tagged(p.dest[d] + static_cast<int64_t>(p.rows_total) * kHD + R, lse);
   }
-  __threadfence_system();
-  __syncwarp();
-  if (lane < p.n_dest)
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.dest_flag[lane] + R), "r"(1u)
-                 : "memory");
 }
 
 // ------------------------------------------------------------------------------------------
@@ -871,8 +876,7 @@ int decode_impl(const SolortDecodeArgs* a, const SolortExchangeArgs* x, void* st
         x->rank >= x->num_ranks)
       return SOLORT_ERR_INVALID_ARGUMENT;
     for (int d = 0; d < x->num_ranks; ++d)
-      if (!aligned(x->slot_in_rank[d], 16) || !aligned(x->flag_in_rank[d], 4))
-        return SOLORT_ERR_INVALID_ARGUMENT;
+      if (!aligned(x->slot_in_rank[d], 16)) return SOLORT_ERR_INVALID_ARGUMENT;
   } else if (partial_out ? !a->out_f32 : !a->out) {
     return SOLORT_ERR_INVALID_ARGUMENT;
   }
@@ -948,10 +952,8 @@ int decode_impl(const SolortDecodeArgs* a, const SolortExchangeArgs* x, void* st
   fill_output_fields(a, &mp.out);
   if (x) {
     mp.n_dest = x->num_ranks;
-    for (int d = 0; d < x->num_ranks; ++d) {
-      mp.dest[d] = x->slot_in_rank[d];
-      mp.dest_flag[d] = x->flag_in_rank[d];
-    }
+    for (int d = 0; d < x->num_ranks; ++d)
+      mp.dest[d] = reinterpret_cast<unsigned long long*>(x->slot_in_rank[d]);
   }
   return launch_merge(mp, stream);
 }

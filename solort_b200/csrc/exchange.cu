@@ -1,13 +1,14 @@
 // Receive side of the sequence-sharded decode exchange, and the exchange buffers.
 //
-// Every rank's merge kernel (decode.cu, exchange mode) stores its partial rows (O fp32 [rows][128],
-// then LSE [rows]) straight into a slot of every rank's receive buffer over NVLink and raises one
-// flag per row there with a system-scope release. exchange_merge_kernel, on each rank, gives one
-// warp to each output row: lanes 0..R-1 each wait (acquire, bounded by one second) for the row's
-// flag from one rank, the warp then reads the R partial rows from its own memory, combines them
-// by log-sum-exp and writes the bf16 row, and finally clears the R flags for the next use of the
-// slots. No collective library runs on this path and no kernel loads from peer memory: peers only
-// store into it.
+// Every rank's merge kernel (decode.cu, exchange mode) stores its partial rows (O [rows][128],
+// then LSE [rows]) straight into a slot of every rank's receive buffer over NVLink, as 64-bit
+// words whose high half is an arrival mark and whose low half is the float (one single-copy-atomic
+// store per word, the scheme of NCCL's low-latency protocol). exchange_merge_kernel, on each rank,
+// gives one warp to each output row: every lane polls its own words of the R slots (relaxed,
+// system-scope loads of this GPU's memory, bounded by one second) until all carry the mark, the
+// warp combines the R partials by log-sum-exp and writes the bf16 row, and the lanes then zero the
+// words they read for the next use of the slots. No fence, flag or collective library is on this
+// path, and no kernel loads from peer memory: peers only store into it.
 //
 // The buffers are plain cudaMalloc allocations exported with CUDA IPC handles, so each process
 // maps its peers' buffers with cudaIpcOpenMemHandle: point-to-point mappings only.
@@ -28,15 +29,20 @@ constexpr int kRowsPerCta = 4;  // one warp per output row
 constexpr unsigned kDevErrPeerTimeout = 1u << 3;
 
 struct Params {
-  const float* slots;  // rank s: slots + s * slot_stride
-  unsigned* flags;     // rank s: flags + s * flag_stride
-  int64_t slot_stride, flag_stride;
+  unsigned long long* slots;  // rank s: slots + s * slot_stride words
+  int64_t slot_stride;
   int num_ranks;
   int rows;
   int q_len, nh;
   bf16* out;
   int64_t o_sb, o_st, o_sh;
 };
+
+__device__ __forceinline__ unsigned long long load_word(const unsigned long long* w) {
+  unsigned long long x;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(x) : "l"(w) : "memory");
+  return x;
+}
 
 __global__ void __launch_bounds__(kRowsPerCta * 32) exchange_merge_kernel(const Params p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -45,64 +51,74 @@ __global__ void __launch_bounds__(kRowsPerCta * 32) exchange_merge_kernel(const 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (row >= p.rows) return;
 
-  // Wait for this row's partial from every rank.
+  // Lane l's words in slot s: O dims 4l..4l+3 of this row, and the row's LSE.
+  float o[SOLORT_MAX_RANKS][4];
+  float lse[SOLORT_MAX_RANKS];
   bool ok = true;
-  if (lane < p.num_ranks) {
-    const unsigned* f = p.flags + lane * p.flag_stride + row;
-    const unsigned long long t0 = globaltimer_ns();
-    unsigned v = 0;
+  const unsigned long long t0 = globaltimer_ns();
+#pragma unroll
+  for (int s = 0; s < SOLORT_MAX_RANKS; ++s) {
+    if (s >= p.num_ranks) break;
+    const unsigned long long* slot = p.slots + s * p.slot_stride;
+    const unsigned long long* wo = slot + static_cast<int64_t>(row) * kHD + lane * 4;
+    const unsigned long long* wl = slot + static_cast<int64_t>(p.rows) * kHD + row;
     for (unsigned i = 0;; ++i) {
-      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-      if (v != 0u) break;
-      if ((i & 63u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+      const unsigned long long x0 = load_word(wo), x1 = load_word(wo + 1), x2 = load_word(wo + 2),
+                               x3 = load_word(wo + 3), xl = load_word(wl);
+      if ((x0 >> 32) & (x1 >> 32) & (x2 >> 32) & (x3 >> 32) & (xl >> 32)) {
+        o[s][0] = __uint_as_float(static_cast<unsigned>(x0));
+        o[s][1] = __uint_as_float(static_cast<unsigned>(x1));
+        o[s][2] = __uint_as_float(static_cast<unsigned>(x2));
+        o[s][3] = __uint_as_float(static_cast<unsigned>(x3));
+        lse[s] = __uint_as_float(static_cast<unsigned>(xl));
+        break;
+      }
+      if ((i & 15u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
         ok = false;
         break;
       }
     }
+    if (!ok) break;
   }
   if (!__all_sync(0xffffffffu, ok)) {
     if (lane == 0) atomicOr(&g_exchange_status, kDevErrPeerTimeout);
-    return;  // flags stay as they are: the host sees the status bit
+    return;  // the slots stay as they are: the host sees the status bit
   }
-  __syncwarp();
 
-  // Log-sum-exp combine of the R partial rows (R <= 8): lane l holds dims 4l..4l+3.
-  float lse[SOLORT_MAX_RANKS];
-  float4 o[SOLORT_MAX_RANKS];
+  // Log-sum-exp combine of the R partial rows: lane l holds dims 4l..4l+3.
   float M = -INFINITY;
 #pragma unroll
-  for (int s = 0; s < SOLORT_MAX_RANKS; ++s) {
-    if (s < p.num_ranks) {
-      const float* slot = p.slots + s * p.slot_stride;
-      lse[s] = __ldcg(slot + static_cast<int64_t>(p.rows) * kHD + row);
-      o[s] = __ldcg(reinterpret_cast<const float4*>(slot + static_cast<int64_t>(row) * kHD) + lane);
-      M = fmaxf(M, lse[s]);
-    }
-  }
-  float D = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < SOLORT_MAX_RANKS; ++s)
+    if (s < p.num_ranks) M = fmaxf(M, lse[s]);
+  float D = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll
   for (int s = 0; s < SOLORT_MAX_RANKS; ++s) {
     if (s < p.num_ranks && lse[s] != -INFINITY) {
       const float w = __expf(lse[s] - M);
       D += w;
-      acc.x += w * o[s].x;
-      acc.y += w * o[s].y;
-      acc.z += w * o[s].z;
-      acc.w += w * o[s].w;
+      a0 += w * o[s][0];
+      a1 += w * o[s][1];
+      a2 += w * o[s][2];
+      a3 += w * o[s][3];
     }
   }
   const float inv = D > 0.f ? __frcp_rn(D) : 0.f;
   const int h = row % p.nh, t = (row / p.nh) % p.q_len, b = row / (p.nh * p.q_len);
   bf16* dst = p.out + b * p.o_sb + t * p.o_st + h * p.o_sh + lane * 4;
   uint2 pk;
-  pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-  pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  pk.x = pack_bf16x2(a0 * inv, a1 * inv);
+  pk.y = pack_bf16x2(a2 * inv, a3 * inv);
   *reinterpret_cast<uint2*>(dst) = pk;
 
-  // Every lane's reads are done: clear the flags for the next use of these slots.
+  // Zero the words this warp read (every lane has its values): the slots are ready for reuse.
   __syncwarp();
-  if (lane < p.num_ranks) p.flags[lane * p.flag_stride + row] = 0u;
+  for (int s = 0; s < p.num_ranks; ++s) {
+    unsigned long long* slot = p.slots + s * p.slot_stride;
+    unsigned long long* wo = slot + static_cast<int64_t>(row) * kHD + lane * 4;
+    *reinterpret_cast<ulonglong2*>(wo) = make_ulonglong2(0ull, 0ull);
+    *reinterpret_cast<ulonglong2*>(wo + 2) = make_ulonglong2(0ull, 0ull);
+    if (lane == 0) slot[static_cast<int64_t>(p.rows) * kHD + row] = 0ull;
+  }
 }
 
 }  // namespace xch
@@ -122,25 +138,23 @@ int read_exchange_status(unsigned* flags) {
 using namespace solort;
 
 extern "C" int solort_attn_exchange_merge(const SolortExchangeMergeArgs* a, void* stream) {
-  if (!a || !a->slots || !a->flags || !a->out) return SOLORT_ERR_INVALID_ARGUMENT;
+  if (!a || !a->slots || !a->out) return SOLORT_ERR_INVALID_ARGUMENT;
   if (a->head_dim != xch::kHD) return SOLORT_ERR_UNSUPPORTED;
   if (a->num_ranks < 1 || a->num_ranks > SOLORT_MAX_RANKS) return SOLORT_ERR_INVALID_ARGUMENT;
   if (a->batch <= 0 || a->q_len <= 0 || a->num_qo_heads <= 0) return SOLORT_ERR_INVALID_ARGUMENT;
-  if (!aligned(a->slots, 16) || !aligned(a->flags, 4) || !aligned(a->out, 8) ||
+  if (!aligned(a->slots, 16) || !aligned(a->out, 8) ||
       (a->out_stride_batch | a->out_stride_token | a->out_stride_head) & 3)
     return SOLORT_ERR_INVALID_ARGUMENT;
   const int64_t rows = static_cast<int64_t>(a->batch) * a->q_len * a->num_qo_heads;
   if (rows > (1ll << 30)) return SOLORT_ERR_UNSUPPORTED;
-  if (a->slot_stride < rows * (xch::kHD + 1) || (a->slot_stride & 3) || a->flag_stride < rows)
+  if (a->slot_stride < rows * (xch::kHD + 1) || (a->slot_stride & 1))
     return SOLORT_ERR_INVALID_ARGUMENT;
   DeviceInfo di;
   int rc = current_device_info(&di);
   if (rc != SOLORT_OK) return rc;
   xch::Params p{};
-  p.slots = a->slots;
-  p.flags = a->flags;
+  p.slots = reinterpret_cast<unsigned long long*>(a->slots);
   p.slot_stride = a->slot_stride;
-  p.flag_stride = a->flag_stride;
   p.num_ranks = a->num_ranks;
   p.rows = static_cast<int>(rows);
   p.q_len = a->q_len;

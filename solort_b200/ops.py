@@ -365,7 +365,7 @@ def gqa_decode_exchange(
     num_splits: int = 0,
 ) -> None:
     """Decode over this rank's key shard and store the rank's partial ``(O, LSE)`` into its slot
-    on every rank named by ``exchange`` (peer-memory stores), raising the rows' flags there."""
+    on every rank named by ``exchange`` (peer-memory stores of self-marking 64-bit words)."""
     cap, nkv, st, sh = _static_kv(k_cache, v_cache, kv_layout)
     a = _decode_args(
         q, k_cache, v_cache, q_pos, stride_token=st, stride_head=sh, stride_page=0,
@@ -385,16 +385,14 @@ def gqa_decode_exchange(
                "solort_attn_decode_exchange")
 
 
-def exchange_merge(slots: int, slot_stride: int, flags: int, flag_stride: int, num_ranks: int,
-                   out: torch.Tensor) -> torch.Tensor:
-    """Wait for every rank's partial in this rank's receive slots / flags (device addresses; rank
-    ``s`` at ``slots + s * slot_stride`` floats and ``flags + s * flag_stride`` words), merge them
-    into bf16 ``out [B, q_len, nh, 128]`` and clear the flags."""
+def exchange_merge(slots: int, slot_stride: int, num_ranks: int, out: torch.Tensor) -> torch.Tensor:
+    """Wait for every rank's partial in this rank's receive slots (device address; rank ``s``'s
+    slot at ``slots + s * slot_stride`` 64-bit words), merge them into bf16 ``out [B, q_len, nh,
+    128]`` and zero the slots for their next use."""
     _check_cuda("out", out, torch.bfloat16)
     B, T, H, D = out.shape
     m = _lib.SolortExchangeMergeArgs()
-    m.slots, m.slot_stride, m.flags, m.flag_stride = slots, slot_stride, flags, flag_stride
-    m.num_ranks = num_ranks
+    m.slots, m.slot_stride, m.num_ranks = slots, slot_stride, num_ranks
     m.batch, m.q_len, m.num_qo_heads, m.head_dim = B, T, H, D
     m.out = out.data_ptr()
     m.out_stride_batch, m.out_stride_token, m.out_stride_head = out.stride(0), out.stride(1), out.stride(2)

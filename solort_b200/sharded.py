@@ -8,11 +8,13 @@ partials reach every rank, and each rank merges the ``R`` of them into the bf16 
 
 Two exchanges:
 
-* ``exchange="p2p"`` (the GPU path ``bench.py`` runs): ``gqa_decode_exchange`` -- the split-KV decode whose merge
-  kernel stores the rank's partial rows straight into its slot on every rank over NVLink and raises
-  a flag per row there -- then ``exchange_merge``, which waits (bounded) for the flags, merges and
-  clears them. The slots live in ``PeerExchange`` buffers: plain allocations exported by CUDA IPC
-  and mapped point to point by every peer. No collective library and no load from peer memory.
+* ``exchange="p2p"`` (the GPU path ``bench.py`` runs): ``gqa_decode_exchange`` -- the split-KV
+  decode whose merge kernel stores the rank's partial rows straight into its slot on every rank
+  over NVLink, as 64-bit words that each carry a float and an arrival mark -- then
+  ``exchange_merge``, which polls its slots (bounded) until every word is marked, merges and zeroes
+  them. The slots live in ``PeerExchange`` buffers: plain allocations exported by CUDA IPC and
+  mapped point to point by every peer. No collective library, fence or flag, and no load from peer
+  memory.
 * ``exchange="nccl"``: ``gqa_decode_partial`` into a packed ``[rows * 129]`` buffer,
   ``torch.distributed.all_gather_into_tensor`` (NCCL over NVLink / NVSwitch), then ``lse_merge``.
   The partial / merge functions are injectable so this rank logic also runs on CPU ranks
@@ -36,22 +38,16 @@ SLOT_FLOATS_PER_ROW = HEAD_DIM + 1  # O row + its LSE
 
 
 def exchange_layout(rank: int, world: int, rows: int, layers: int) -> dict:
-    """Byte layout of one rank's exchange buffer: ``[layers][world]`` slots of ``rows * 129`` fp32
-    (padded to 256 bytes, so every slot is 16-byte aligned), then ``[layers][world][rows]`` uint32
-    flags. Slot ``(li, src)`` receives rank ``src``'s partial for layer ``li``. Returns the sizes
-    and two offset functions."""
-    slot_bytes = -(-rows * SLOT_FLOATS_PER_ROW * 4 // 256) * 256
-    data_bytes = -(-layers * world * slot_bytes // 256) * 256
-    flag_bytes = layers * world * rows * 4
+    """Byte layout of one rank's exchange buffer: ``[layers][world]`` slots of ``rows * 129``
+    64-bit words (each a float plus its arrival mark), padded to 256 bytes so every slot is
+    16-byte aligned. Slot ``(li, src)`` receives rank ``src``'s partial for layer ``li``. Returns
+    the sizes and the slot offset function."""
+    slot_bytes = -(-rows * SLOT_FLOATS_PER_ROW * 8 // 256) * 256
 
     def slot(li: int, src: int) -> int:
         return (li * world + src) * slot_bytes
 
-    def flags(li: int, src: int) -> int:
-        return data_bytes + (li * world + src) * rows * 4
-
-    return {"slot_bytes": slot_bytes, "data_bytes": data_bytes, "flag_bytes": flag_bytes,
-            "total_bytes": data_bytes + flag_bytes, "slot": slot, "flags": flags}
+    return {"slot_bytes": slot_bytes, "total_bytes": layers * world * slot_bytes, "slot": slot}
 
 
 class PeerExchange:
@@ -106,15 +102,12 @@ class PeerExchange:
         x.num_ranks, x.rank = self.world, self.rank
         for p in range(self.world):
             x.slot_in_rank[p] = self.base[p] + self.layout["slot"](li, self.rank)
-            x.flag_in_rank[p] = self.base[p] + self.layout["flags"](li, self.rank)
         return x
 
-    def recv(self, li: int) -> tuple[int, int, int, int]:
-        """This rank's receive slots and flags for layer ``li``: (slot address, slot stride in
-        floats, flag address, flag stride in words), rank ``s`` at ``+ s * stride``."""
-        lay = self.layout
-        return (self.own + lay["slot"](li, 0), lay["slot_bytes"] // 4,
-                self.own + lay["flags"](li, 0), self.rows)
+    def recv(self, li: int) -> tuple[int, int]:
+        """This rank's receive slots for layer ``li``: (address, stride in 64-bit words), rank
+        ``s``'s slot at ``address + s * stride`` words."""
+        return self.own + self.layout["slot"](li, 0), self.layout["slot_bytes"] // 8
 
     @classmethod
     def emulate(cls, world: int, rows: int, layers: int) -> list["PeerExchange"]:

@@ -109,19 +109,18 @@ def test_rank_failure_before_collective_is_reported_not_hung():
 
 @pytest.mark.parametrize("world,rows,layers", [(1, 32, 36), (2, 32, 36), (8, 32, 36), (3, 5, 4)])
 def test_exchange_layout_slots_are_aligned_and_disjoint(world, rows, layers):
-    """The peer-exchange buffer: every slot 16-byte aligned (float4 stores), slots and flag
-    blocks never overlap, and all of them fit in the allocation."""
+    """The peer-exchange buffer: every slot 16-byte aligned (vector stores), slots never overlap,
+    and all of them fit in the allocation."""
     from solort_b200.sharded import SLOT_FLOATS_PER_ROW, exchange_layout
 
     lay = exchange_layout(0, world, rows, layers)
-    assert lay["slot_bytes"] >= rows * SLOT_FLOATS_PER_ROW * 4
+    assert lay["slot_bytes"] >= rows * SLOT_FLOATS_PER_ROW * 8
     spans = []
     for li in range(layers):
         for src in range(world):
             s = lay["slot"](li, src)
-            f = lay["flags"](li, src)
-            assert s % 16 == 0 and f % 4 == 0
-            spans += [(s, s + rows * SLOT_FLOATS_PER_ROW * 4), (f, f + rows * 4)]
+            assert s % 16 == 0
+            spans.append((s, s + rows * SLOT_FLOATS_PER_ROW * 8))
     spans.sort()
     for (a0, a1), (b0, _) in zip(spans, spans[1:]):
         assert a1 <= b0
