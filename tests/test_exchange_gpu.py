@@ -2,10 +2,11 @@
 
 Each emulated rank owns a shard of the keys and an exchange buffer in this GPU's memory. All R
 ranks' sends (``gqa_decode_exchange``: decode over the shard, then stores of the rank's partial
-into its slot on every rank plus per-row flags) run before any rank's ``exchange_merge``, so every
-flag a merge waits for is already set: no kernel ever waits on one that has not finished. The merged
-output of every rank must match the oracle's attention over the whole sequence (max-abs <= 2e-2,
-mean-abs <= 2e-3), on two rounds in a row (the merges clear the flags for the next round).
+into its slot on every rank as self-marking 64-bit words) run before any rank's ``exchange_merge``,
+so every word a merge waits for is already there: no kernel ever waits on one that has not
+finished. The merged output of every rank must match the oracle's attention over the whole sequence
+(max-abs <= 2e-2, mean-abs <= 2e-3), on two rounds in a row (the merges zero the slots for the
+next round).
 """
 
 from __future__ import annotations

@@ -1,5 +1,5 @@
 """The peer-memory exchange across real GPUs: one process per GPU, each mapping the others'
-exchange buffers through CUDA IPC, NVLink stores of every rank's partial, bounded flag waits.
+exchange buffers through CUDA IPC, NVLink stores of every rank's partial, bounded waits.
 
 Runs only where the process sees at least two GPUs (skipped otherwise; ranks never share a GPU,
 since a kernel must not wait on another launch on the same GPU). The handle exchange and the
