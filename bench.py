@@ -310,10 +310,13 @@ def run_gpu_arm(args) -> None:
     if sharded is None:
         calls = [ops.DecodeCall(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND",
                                 out=outs[li], workspace=ws) for li in range(LAYERS)]
+    elif args.exchange == "p2p":
+        calls = [sharded.prepared_layer(li, q[li], kv[li, 0], kv[li, 1], qpos, rank * ctx,
+                                        outs[li], ws) for li in range(LAYERS)]
 
     def e2e_step():
         q.copy_(q_host, non_blocking=True)
-        if sharded is None:
+        if calls:
             for c in calls:
                 c()
         else:
@@ -368,7 +371,8 @@ def run_gpu_arm(args) -> None:
             "keys_per_gpu": ctx, "context": ctx * world,
             "kv_layout": "[layer, 2, nkv, max_len, hd] bf16",
             "parallelism": f"seq-shard x{world}" if world > 1 else "single GPU",
-            "exchange": (("NVLink peer stores + flag-synchronised merge" if args.exchange == "p2p"
+            "exchange": (("NVLink peer stores of self-marking words + polling merge kernel"
+                          if args.exchange == "p2p"
                           else "NCCL all_gather_into_tensor + lse_merge") if world > 1 else None),
             "l2": "inputs larger than L2: 36 layers x 32 MiB KV per GPU replayed in order",
             "graph": "36 layer calls per CUDA graph replay",
@@ -393,10 +397,18 @@ def run_gpu_arm(args) -> None:
                 "h2d_bytes_per_step": q_host.numel() * 2,
                 "d2h_bytes_per_step": out_host.numel() * 2,
                 "ms_per_step": round(e2e_ms, 4),
-                "how": "ops.DecodeCall per layer from Python, pinned H2D of the 36 queries and "
+                "how": ("ops.DecodeCall" if world == 1 else
+                        "ops.ShardedDecodeCall (decode + peer exchange + merge)" if calls else
+                        "ShardedDecode.layer")
+                       + " per layer from Python, pinned H2D of the 36 queries and "
                        "D2H of the 36 outputs inside the timed region"},
         "gpu_launches": LAYERS * (2 if world == 1 else 3) * args.steps,
-        "gpu_launches_note": "timed region: 36 decode_kernel + 36 merge_kernel launches per step",
+        "gpu_launches_note": ("timed region: 36 decode_kernel + 36 merge_kernel launches per step"
+                              if world == 1 else
+                              "timed region per step: 36 x (decode_kernel + merge_kernel sending "
+                              "to every rank + exchange_merge_kernel)" if args.exchange == "p2p"
+                              else "timed region per step: 36 x (decode_kernel + merge_kernel + "
+                              "lse merge), NCCL all-gather kernels not counted"),
         "clocks": clk,
     }
     if sweep:

@@ -212,6 +212,52 @@ class DecodeCall:
             _lib.check(rc, "solort_attn_decode")
 
 
+class ShardedDecodeCall:
+    """A prepared sharded-decode layer on fixed buffers: ``gqa_decode_exchange`` over this rank's
+    shard followed by ``exchange_merge``, both packed once, each call two C-ABI launches on the
+    current stream."""
+
+    def __init__(self, q, k_shard, v_shard, q_pos, exchange, recv_slots: int, slot_stride: int,
+                 num_ranks: int, *, kv_pos_offset=0, kv_layout="NHD", scale=None, out,
+                 workspace):
+        cap, nkv, st, sh = _static_kv(k_shard, v_shard, kv_layout)
+        _check_cuda("out", out, torch.bfloat16)
+        self._keep = (q, k_shard, v_shard, q_pos, out, workspace, exchange)
+        self.args = _decode_args(
+            q, k_shard, v_shard, q_pos, stride_token=st, stride_head=sh, stride_page=0,
+            kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
+            scale=scale, max_kv_len=cap, out=None, out_f32=None, lse_out=None, q_lens=None,
+            kv_pos_offset=kv_pos_offset, num_splits=0)
+        lib = _lib.load()
+        need = ctypes.c_size_t(0)
+        _lib.check(lib.solort_attn_decode_exchange_workspace_size(ctypes.byref(self.args),
+                                                                  ctypes.byref(need)),
+                   "solort_attn_decode_exchange_workspace_size")
+        if workspace.numel() * workspace.element_size() < need.value:
+            raise RuntimeError(f"ShardedDecodeCall needs a workspace of {need.value} bytes")
+        self.args.workspace = workspace.data_ptr()
+        self.args.workspace_bytes = workspace.numel() * workspace.element_size()
+        B, T, H, D = out.shape
+        self.margs = _lib.SolortExchangeMergeArgs()
+        self.margs.slots, self.margs.slot_stride, self.margs.num_ranks = recv_slots, slot_stride, num_ranks
+        self.margs.batch, self.margs.q_len, self.margs.num_qo_heads, self.margs.head_dim = B, T, H, D
+        self.margs.out = out.data_ptr()
+        self.margs.out_stride_batch, self.margs.out_stride_token, self.margs.out_stride_head = (
+            out.stride(0), out.stride(1), out.stride(2))
+        self._send, self._merge = lib.solort_attn_decode_exchange, lib.solort_attn_exchange_merge
+        self._a, self._x, self._m = ctypes.byref(self.args), ctypes.byref(exchange), ctypes.byref(self.margs)
+        self._device = q.device
+
+    def __call__(self) -> None:
+        st = ctypes.c_void_p(torch.cuda.current_stream(self._device).cuda_stream)
+        rc = self._send(self._a, self._x, st)
+        if rc != 0:
+            _lib.check(rc, "solort_attn_decode_exchange")
+        rc = self._merge(self._m, st)
+        if rc != 0:
+            _lib.check(rc, "solort_attn_exchange_merge")
+
+
 def gqa_decode_partial(
     q: torch.Tensor,
     k_cache: torch.Tensor,

@@ -199,6 +199,19 @@ class ShardedDecode:
             self.recv[li].copy_(buf)
         return self.merge_fn(o_parts, lse_parts, out=out)
 
+    def prepared_layer(self, li: int, q: torch.Tensor, k_shard: torch.Tensor,
+                       v_shard: torch.Tensor, q_pos: torch.Tensor, kv_pos_offset: int,
+                       out: torch.Tensor, workspace: torch.Tensor):
+        """``layer`` with its arguments packed once (peer exchange only): a callable that launches
+        the layer's two kernels on the current stream."""
+        from solort_b200 import ops
+
+        if self.px is None:
+            raise RuntimeError("prepared layers need exchange='p2p'")
+        return ops.ShardedDecodeCall(q, k_shard, v_shard, q_pos, self.px.send_args[li],
+                                     *self.px.recv(li), self.world, kv_pos_offset=kv_pos_offset,
+                                     kv_layout=self.kv_layout, out=out, workspace=workspace)
+
     def close(self) -> None:
         if self.px is not None:
             self.px.close()
