@@ -240,6 +240,49 @@ typedef struct SolortPrefillArgs {
 
 SOLORT_API int solort_attn_prefill(const SolortPrefillArgs* args, void* stream);
 
+/*
+ * Attention prologue of one layer (decode, verify or prefill): per-head QK-RMSNorm and rotate-half
+ * RoPE of the fused QKV projection, the normalised queries written to q_out, and this step's K / V
+ * rows appended to the cache. Replaces src/solort/model/cuda_graph_executor.py:176-179 (decode),
+ * :120-123 (prefill) and :257-260 (verify): _rmsnorm (:25-28), _rope (:100-102) with the bf16
+ * _cos_sin tables (:95-98), and the index_copy_ / slice stores into kc/vc; with a block table, the
+ * slot-mapped store of src/solort/cache/kv_cache.py:136-149,191-235.
+ *   qkv      [num_tokens, (nqo + 2*nkv) * 128] bf16: query heads, then key heads, then value heads
+ *   q/k_norm_weight [128] bf16; eps as the model's rms_norm_eps
+ *   cos, sin [rope_rows, 128] bf16: the model's tables by position (row p = _cos_sin(p))
+ *   pos      int64 [1] on the device: token i sits at position pos[0] + i
+ *   q_out    token i, head h at q_out + i*q_out_stride_token + h*q_out_stride_head (bf16)
+ *   k/v_cache static: row (position p, kv head h) at + p*kv_stride_token + h*kv_stride_head,
+ *            kv_capacity rows; paged (block_table != NULL): page bt[p / page_size], row
+ *            p % page_size at + page*kv_stride_page + row*kv_stride_token + h*kv_stride_head,
+ *            kv_capacity = num_pages * page_size. Positions past kv_capacity are not stored.
+ * Rounding follows the reference step by step except the fp32 sum of squares, a warp tree.
+ * Pointers 8-byte aligned, strides multiples of 4 elements.
+ */
+typedef struct SolortPrologueArgs {
+  const void* qkv;
+  int64_t qkv_stride_token;
+  int32_t num_tokens, num_qo_heads, num_kv_heads, head_dim;
+  const void* q_norm_weight;
+  const void* k_norm_weight;
+  float eps;
+  const void* cos;
+  const void* sin;
+  int64_t rope_stride;
+  int32_t rope_rows;
+  const int64_t* pos;
+  void* q_out;
+  int64_t q_out_stride_token, q_out_stride_head;
+  void* k_cache;
+  void* v_cache;
+  int64_t kv_stride_token, kv_stride_head, kv_stride_page;
+  int32_t kv_capacity;
+  const int32_t* block_table;
+  int32_t page_size;
+} SolortPrologueArgs;
+
+SOLORT_API int solort_attn_qk_norm_rope_append(const SolortPrologueArgs* args, void* stream);
+
 /* Reads and clears the device status word of the current device (bit 0: an in-kernel wait hit
  * its time limit and the kernel returned without writing its output; bit 1: a tensor-memory
  * allocation wait hit its limit; bit 2: a kernel found its shared memory misaligned and returned

@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "solort_attn_exchange_buffer_open",
     "solort_attn_exchange_buffer_close",
     "solort_attn_exchange_buffer_destroy",
+    "solort_attn_qk_norm_rope_append",
 )
 
 MAX_RANKS = 8  # SOLORT_MAX_RANKS
@@ -122,6 +123,32 @@ class SolortExchangeMergeArgs(ctypes.Structure):
     ]
 
 
+class SolortPrologueArgs(ctypes.Structure):
+    """Mirror of ``SolortPrologueArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("qkv", c_vp),
+        ("qkv_stride_token", c_i64),
+        ("num_tokens", c_i32), ("num_qo_heads", c_i32), ("num_kv_heads", c_i32), ("head_dim", c_i32),
+        ("q_norm_weight", c_vp),
+        ("k_norm_weight", c_vp),
+        ("eps", c_f32),
+        ("cos", c_vp),
+        ("sin", c_vp),
+        ("rope_stride", c_i64),
+        ("rope_rows", c_i32),
+        ("pos", c_vp),
+        ("q_out", c_vp),
+        ("q_out_stride_token", c_i64), ("q_out_stride_head", c_i64),
+        ("k_cache", c_vp),
+        ("v_cache", c_vp),
+        ("kv_stride_token", c_i64), ("kv_stride_head", c_i64), ("kv_stride_page", c_i64),
+        ("kv_capacity", c_i32),
+        ("block_table", c_vp),
+        ("page_size", c_i32),
+    ]
+
+
 _LIB: ctypes.CDLL | None = None
 
 
@@ -174,6 +201,8 @@ def _optional_symbols(lib: ctypes.CDLL) -> None:
     lib.solort_attn_exchange_buffer_close.restype = ctypes.c_int
     lib.solort_attn_exchange_buffer_destroy.argtypes = [c_vp]
     lib.solort_attn_exchange_buffer_destroy.restype = ctypes.c_int
+    lib.solort_attn_qk_norm_rope_append.argtypes = [P(SolortPrologueArgs), c_vp]
+    lib.solort_attn_qk_norm_rope_append.restype = ctypes.c_int
 
 
 class SolortPrefillArgs(ctypes.Structure):

@@ -447,6 +447,66 @@ def exchange_merge(slots: int, slot_stride: int, num_ranks: int, out: torch.Tens
     return out
 
 
+def qk_norm_rope_append(
+    qkv: torch.Tensor,
+    q_norm_weight: torch.Tensor,
+    k_norm_weight: torch.Tensor,
+    eps: float,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    pos: torch.Tensor,
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    *,
+    num_qo_heads: int,
+    num_kv_heads: int,
+    q_out: torch.Tensor | None = None,
+    block_table: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One layer's attention prologue: QK-RMSNorm + RoPE of ``qkv [t, (nh + 2 nkv) * 128]``,
+    queries to ``q_out [t, nh, 128]``, K / V appended at positions ``pos[0] .. pos[0] + t - 1``.
+
+    ``k_cache``/``v_cache``: one layer's static NHD buffers ``[max_len, nkv, 128]`` (the reference's
+    ``kc[li]``/``vc[li]``), or with ``block_table`` (int32, the sequence's physical pages) the K / V
+    halves of a paged arena, ``arena[:, 0]`` / ``arena[:, 1]`` of ``[pages, 2, P, nkv, 128]``.
+    ``cos``/``sin``: the model's bf16 tables ``[rows, 128]`` indexed by position."""
+    _check_cuda("qkv", qkv, torch.bfloat16)
+    t = qkv.shape[0]
+    if qkv.dim() != 2 or qkv.shape[1] != (num_qo_heads + 2 * num_kv_heads) * HEAD_DIM or qkv.stride(1) != 1:
+        raise RuntimeError("qkv must be [t, (num_qo_heads + 2 * num_kv_heads) * 128], rows contiguous")
+    for name, tsr in (("cos", cos), ("sin", sin)):
+        _check_cuda(name, tsr, torch.bfloat16)
+        if tsr.dim() != 2 or tsr.shape[1] != HEAD_DIM or tsr.stride(1) != 1:
+            raise RuntimeError(f"{name} must be [rows, 128] with contiguous rows")
+    _check_cuda("pos", pos, torch.int64)
+    if q_out is None:
+        q_out = torch.empty(t, num_qo_heads, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
+    a = _lib.SolortPrologueArgs()
+    a.qkv, a.qkv_stride_token = qkv.data_ptr(), qkv.stride(0)
+    a.num_tokens, a.num_qo_heads, a.num_kv_heads, a.head_dim = t, num_qo_heads, num_kv_heads, HEAD_DIM
+    a.q_norm_weight, a.k_norm_weight, a.eps = q_norm_weight.data_ptr(), k_norm_weight.data_ptr(), float(eps)
+    a.cos, a.sin, a.rope_stride, a.rope_rows = cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.shape[0]
+    a.pos = pos.data_ptr()
+    a.q_out, a.q_out_stride_token, a.q_out_stride_head = q_out.data_ptr(), q_out.stride(0), q_out.stride(1)
+    a.k_cache, a.v_cache = k_cache.data_ptr(), v_cache.data_ptr()
+    if block_table is None:
+        if k_cache.dim() != 3 or k_cache.stride() != v_cache.stride():
+            raise RuntimeError("static k_cache / v_cache must be [max_len, nkv, 128] with equal strides")
+        a.kv_stride_token, a.kv_stride_head, a.kv_stride_page = k_cache.stride(0), k_cache.stride(1), 0
+        a.kv_capacity = k_cache.shape[0]
+    else:
+        _check_cuda("block_table", block_table, torch.int32)
+        if k_cache.dim() != 4 or k_cache.stride() != v_cache.stride():
+            raise RuntimeError("paged k_cache / v_cache must be [pages, P, nkv, 128] views with equal strides")
+        P = k_cache.shape[1]
+        a.kv_stride_page, a.kv_stride_token, a.kv_stride_head = k_cache.stride(0), k_cache.stride(1), k_cache.stride(2)
+        a.kv_capacity = block_table.numel() * P  # positions the table covers
+        a.block_table, a.page_size = block_table.data_ptr(), P
+    _lib.check(_lib.load().solort_attn_qk_norm_rope_append(ctypes.byref(a), ctypes.c_void_p(_stream(qkv.device))),
+               "solort_attn_qk_norm_rope_append")
+    return q_out
+
+
 def device_status() -> int:
     """Read and clear the library's device status word (nonzero: an in-kernel wait timed out)."""
     flags = ctypes.c_uint(0)

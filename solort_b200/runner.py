@@ -13,8 +13,11 @@ What changes is the attention at the three inline sites:
   the live position from ``pos_buf`` on the device (split-KV, fp32 softmax);
 * verify (``:250, 261-263``, ``repeat_interleave`` of the whole buffer + masked SDPA) ->
   ``ops.gqa_decode`` with ``q_len = K + 1`` (per-row causal limit, no expansion).
-Everything else (weights fusion, norms, RoPE, KV appends, MLP, lm_head, argmax) is the same math
-as the reference, so greedy streams differ only where attention numerics do.
+With ``prologue="fused"`` (the default) the per-head QK-RMSNorm, RoPE and KV append of each
+layer (``:176-179, 120-123, 257-260``) run as one ``ops.qk_norm_rope_append`` launch reading the
+model's bf16 cos/sin tables; ``prologue="torch"`` keeps the reference's torch ops there.
+Everything else (weights fusion, input / post norms, MLP, lm_head, argmax) is the same math as the
+reference.
 """
 
 from __future__ import annotations
@@ -34,7 +37,10 @@ def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 class GraphQwen3Runner:
     MAX_VERIFY_TOKENS = 8
 
-    def __init__(self, model, max_len: int) -> None:
+    def __init__(self, model, max_len: int, prologue: str = "fused") -> None:
+        if prologue not in ("fused", "torch"):
+            raise ValueError(prologue)
+        self.prologue = prologue
         c = model.config
         self.dev = next(model.parameters()).device
         if self.dev.type != "cuda":
@@ -66,6 +72,9 @@ class GraphQwen3Runner:
             })
         theta = float(getattr(c, "rope_theta", None) or c.rope_parameters["rope_theta"])
         self.inv_freq = 1.0 / (theta ** (torch.arange(0, self.hd, 2, device=self.dev).float() / self.hd))
+        # the reference's bf16 cos/sin rows for every position, read by the fused prologue
+        self.cos_tab, self.sin_tab = self._cos_sin(torch.arange(int(max_len), device=self.dev))
+        self.zero_pos = torch.zeros(1, dtype=torch.long, device=self.dev)
         shape = (self.L, self.max_len, self.nkv, self.hd)
         self.kc = torch.zeros(shape, device=self.dev, dtype=self.dt)
         self.vc = torch.zeros(shape, device=self.dev, dtype=self.dt)
@@ -113,6 +122,21 @@ class GraphQwen3Runner:
         k = self._rope(_rmsnorm(k, ly["kn"], self.eps), cos, sin)
         return q, k, v  # [heads, t, hd]
 
+    def _attn_inputs(self, x: torch.Tensor, ly: dict, li: int, t: int, pos_t: torch.Tensor,
+                     pos_rows: torch.Tensor, cos, sin) -> torch.Tensor:
+        """Queries ``[t, nh, hd]`` of layer ``li`` for tokens at ``pos_t[0] ..``, with the tokens' K / V
+        appended to ``kc[li]``/``vc[li]`` (``pos_rows``: the same positions as a vector)."""
+        if self.prologue == "fused":
+            h = _rmsnorm(x, ly["in_ln"], self.eps)
+            qkv = h @ ly["wqkv"].T
+            return ops.qk_norm_rope_append(qkv, ly["qn"], ly["kn"], self.eps, self.cos_tab,
+                                           self.sin_tab, pos_t, self.kc[li], self.vc[li],
+                                           num_qo_heads=self.nh, num_kv_heads=self.nkv)
+        q, k, v = self._qkv(x, ly, t, cos, sin)
+        self.kc[li].index_copy_(0, pos_rows, k.transpose(0, 1))
+        self.vc[li].index_copy_(0, pos_rows, v.transpose(0, 1))
+        return q.transpose(0, 1)
+
     def _mlp(self, x: torch.Tensor, ly: dict) -> torch.Tensor:
         h2 = _rmsnorm(x, ly["post_ln"], self.eps)
         gate, up = (h2 @ ly["wgu"].T).split([self.inter, self.inter], dim=-1)
@@ -121,15 +145,12 @@ class GraphQwen3Runner:
     # ---- prefill ----
     def _prefill_forward(self, bound: int) -> torch.Tensor:
         t = bound
-        cos, sin = self._cos_sin(torch.arange(t, device=self.dev))
+        rows = torch.arange(t, device=self.dev)
+        cos, sin = (None, None) if self.prologue == "fused" else self._cos_sin(rows)
         x = self.embed[self.pre_tok[:bound]].to(self.dt)
         for li, ly in enumerate(self.layers):
-            q, k, v = self._qkv(x, ly, t, cos, sin)
-            k_t, v_t = k.transpose(0, 1), v.transpose(0, 1)  # [t, nkv, hd]
-            self.kc[li, :t] = k_t
-            self.vc[li, :t] = v_t
-            ctx = ops.gqa_prefill(q.transpose(0, 1), self.kc[li, :t], self.vc[li, :t],
-                                  causal=True, scale=self.scale)
+            q = self._attn_inputs(x, ly, li, t, self.zero_pos, rows, cos, sin)  # [t, nh, hd]
+            ctx = ops.gqa_prefill(q, self.kc[li, :t], self.vc[li, :t], causal=True, scale=self.scale)
             x = x + ctx.reshape(t, self.q_dim) @ ly["wo"].T
             x = self._mlp(x, ly)
         return _rmsnorm(x, self.final_norm, self.eps)
@@ -158,12 +179,10 @@ class GraphQwen3Runner:
 
     # ---- decode ----
     def _decode_forward(self, bound: int) -> torch.Tensor:
-        cos, sin = self._cos_sin(self.pos_buf)
+        cos, sin = (None, None) if self.prologue == "fused" else self._cos_sin(self.pos_buf)
         x = self.embed[self.tok_buf].to(self.dt)
         for li, ly in enumerate(self.layers):
-            q, k, v = self._qkv(x, ly, 1, cos, sin)
-            self.kc[li].index_copy_(0, self.pos_buf, k.transpose(0, 1))
-            self.vc[li].index_copy_(0, self.pos_buf, v.transpose(0, 1))
+            q = self._attn_inputs(x, ly, li, 1, self.pos_buf, self.pos_buf, cos, sin)
             ctx = ops.gqa_decode(q.reshape(1, 1, self.nh, self.hd), self.kc[li], self.vc[li],
                                  self.pos_buf, scale=self.scale, max_kv_len=bound,
                                  workspace=self.attn_ws)
@@ -222,13 +241,11 @@ class GraphQwen3Runner:
     def _verify_forward(self) -> torch.Tensor:
         k1 = self.vtok.shape[0]
         pos = self.vpos0 + torch.arange(k1, device=self.dev)
-        cos, sin = self._cos_sin(pos)
+        cos, sin = (None, None) if self.prologue == "fused" else self._cos_sin(pos)
         x = self.embed[self.vtok].to(self.dt)
         for li, ly in enumerate(self.layers):
-            q, k, v = self._qkv(x, ly, k1, cos, sin)
-            self.kc[li].index_copy_(0, pos, k.transpose(0, 1))
-            self.vc[li].index_copy_(0, pos, v.transpose(0, 1))
-            ctx = ops.gqa_decode(q.transpose(0, 1).reshape(1, k1, self.nh, self.hd), self.kc[li],
+            q = self._attn_inputs(x, ly, li, k1, self.vpos0, pos, cos, sin)
+            ctx = ops.gqa_decode(q.reshape(1, k1, self.nh, self.hd), self.kc[li],
                                  self.vc[li], self.vpos0, scale=self.scale, workspace=self.attn_ws)
             x = x + ctx.reshape(k1, self.q_dim) @ ly["wo"].T
             x = self._mlp(x, ly)

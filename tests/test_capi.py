@@ -67,7 +67,8 @@ def _c_layout(struct: str, fields: list[str]) -> dict[str, int]:
 
 STRUCTS = [(_lib.SolortDecodeArgs, "SolortDecodeArgs"), (_lib.SolortMergeArgs, "SolortMergeArgs"),
            (_lib.SolortExchangeArgs, "SolortExchangeArgs"),
-           (_lib.SolortExchangeMergeArgs, "SolortExchangeMergeArgs")]
+           (_lib.SolortExchangeMergeArgs, "SolortExchangeMergeArgs"),
+           (_lib.SolortPrologueArgs, "SolortPrologueArgs")]
 
 
 @pytest.mark.parametrize("cls,name", STRUCTS + ([(_lib.SolortPrefillArgs, "SolortPrefillArgs")]
