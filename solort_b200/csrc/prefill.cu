@@ -73,8 +73,8 @@ enum {
   kBarSFull = kBarVEmpty + kStages,  // +buffer (2): QK_j committed
   kBarPFull = kBarSFull + 2,         // 256 arrivals: P_j written to TMEM
   kBarPVDone = kBarPFull + 1,        // PV_j committed
-  kBarXMax = kBarPVDone + 1,         // +parity (2), 256 arrivals: row-max exchange
-  kBarXSum = kBarXMax + 2,           // 256 arrivals: final row-sum exchange
+  kBarXMax = kBarPVDone + 1,         // +parity*4 + warp pair (8), 64 arrivals: row-max exchange
+  kBarXSum = kBarXMax + 8,           // 256 arrivals: final row-sum exchange
   kNumBars = kBarXSum + 1
 };
 
@@ -256,7 +256,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       const uint32_t count =
-          (i == kBarPFull || i == kBarXMax || i == kBarXMax + 1 || i == kBarXSum) ? kSoftmaxThreads : 1u;
+          (i == kBarPFull || i == kBarXSum) ? kSoftmaxThreads
+          : (i >= kBarXMax && i < kBarXMax + 8) ? 64u
+                                                 : 1u;
       mbar_init(&bars[i], count);
     }
     *abort_flag = 0;
@@ -400,10 +402,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 8; i < 64; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
       float pmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                          fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      // exchange partial maxima with the other group (double-buffered by tile parity)
+      // exchange partial maxima with the other group (double-buffered by tile parity): only the
+      // two warps that hold these 32 rows (warp 4+w of group 0, 8+w of group 1) meet here
       xmax[(b * 2 + g) * kBM + r] = pmax;
-      mbar_arrive(&bars[kBarXMax + b]);
-      if (!__all_sync(0xffffffffu, wait_bar(&bars[kBarXMax + b], (j >> 1) & 1, abort_flag))) {
+      const int xbar = kBarXMax + b * 4 + ((warp - 4) & 3);
+      mbar_arrive(&bars[xbar]);
+      if (!__all_sync(0xffffffffu, wait_bar(&bars[xbar], (j >> 1) & 1, abort_flag))) {
         ok = false;
         break;
       }
