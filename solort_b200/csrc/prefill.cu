@@ -44,6 +44,7 @@ constexpr int kThreads = 384;
 constexpr int kSoftmaxThreads = 256;         // two warp groups
 constexpr int kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;          // lazy rescale threshold (factor 256)
+constexpr int kPingPongMinTiles = 16;        // 128-row query tiles from which two go per CTA
 
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int kOffQ = 0;
@@ -388,12 +389,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool need_mask =
           (p.causal && j * kBN + kBN - 1 > offset + q0) || (j * kBN + kBN > p.kv_len);
       if (need_mask) {
-        const int k0 = j * kBN + 64 * g;
+        // keys j*128 + 64g + i with i >= nv are past the sequence or above the causal limit
+        const int lim = p.causal ? min(p.kv_len, row_limit + 1) : p.kv_len;
+        const int nv = lim - (j * kBN + 64 * g);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const int key = k0 + i;
-          sv[i] = (key < p.kv_len && (!p.causal || key <= row_limit)) ? sv[i] : -INFINITY;
-        }
+        for (int i = 0; i < 64; ++i) sv[i] = i < nv ? sv[i] : -INFINITY;
       }
       float mx8[8];
 #pragma unroll
@@ -524,6 +524,353 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// Ping-pong variant for long prompts: one CTA computes TWO 128-row query tiles (A = rows
+// q0..q0+127, B = the next 128) of one head against one stream of K/V tiles. TMEM holds S_A, O_A,
+// S_B, O_B (128 columns each); P_x is written over the first 64 columns of S_x. Each tile has its
+// own softmax warp group (warps 4-7 for A, 8-11 for B), thread r owning the whole 128-key row r, so
+// no values are exchanged between groups. The MMA warp interleaves the tiles:
+//   QK_A(0) QK_B(0) | PV_A(j) QK_A(j+1) PV_B(j) QK_B(j+1) | ...
+// so while group A turns S_A(j) into P_A(j) the tensor core runs PV_B(j-1) and QK_B(j), and the
+// other way round: one tile's MMAs and TMEM load latency hide under the other tile's softmax.
+// QK_x(j+1) is issued after PV_x(j) (which reads P_x(j) out of S_x); the MMAs of one CTA run in
+// issue order. K/V tiles are shared by both query tiles (half the K/V traffic per query of the
+// one-tile kernel). Every wait is bounded; the abort path drains like the one-tile kernel.
+namespace pp {
+
+constexpr int kRows = 2 * kBM;                   // query rows per CTA
+constexpr int kOffQA = 0;
+constexpr int kOffQB = kOffQA + kTileBytes;
+constexpr int kOffK = kOffQB + kTileBytes;
+constexpr int kOffV = kOffK + kStages * kTileBytes;
+constexpr int kOffBar = kOffV + kStages * kTileBytes;
+constexpr int kSmemBytes = 1024 + kOffBar + 512;
+
+enum {
+  kBarQ = 0,
+  kBarKFull = 1,                      // +stage
+  kBarKEmpty = kBarKFull + kStages,
+  kBarVFull = kBarKEmpty + kStages,
+  kBarVEmpty = kBarVFull + kStages,
+  kBarSFull = kBarVEmpty + kStages,   // +tile (A, B): QK_x(j) committed
+  kBarPFull = kBarSFull + 2,          // +tile, 128 arrivals: P_x(j) in TMEM
+  kBarPVDone = kBarPFull + 2,         // +tile: PV_x(j) committed
+  kNumBars = kBarPVDone + 2
+};
+
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_pp_kernel(const __grid_constant__ CUtensorMap tmQ,
+                      const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // issue / commit counts for the abort drain: K, V, QK_A, QK_B, PV_A, PV_B
+  volatile int* counts = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  const uint32_t sbase = smem_u32(smem);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pair_tiles = (p.q_tiles + 1) / 2;
+  const int q_pair = pair_tiles - 1 - static_cast<int>(blockIdx.x) / p.nh;  // heaviest first
+  const int head = static_cast<int>(blockIdx.x) % p.nh;
+  const int kvh = head / p.group;
+  const int q0 = q_pair * kRows;
+  const int offset = p.kv_len - p.q_len;  // bottom-right alignment
+  const int kv_tiles_all = (p.kv_len + kBN - 1) / kBN;
+  int n_t[2];  // KV tiles each query tile needs (0 for a tile past the prompt)
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int first = q0 + x * kBM;
+    if (first >= p.q_len) {
+      n_t[x] = 0;
+    } else if (!p.causal) {
+      n_t[x] = kv_tiles_all;
+    } else {
+      const int last_key = offset + min(first + kBM, p.q_len) - 1;
+      n_t[x] = min(kv_tiles_all, last_key / kBN + 1);
+    }
+  }
+  const int n = max(n_t[0], n_t[1]);
+
+  if (tid == 0) {
+    for (int i = 0; i < kNumBars; ++i)
+      mbar_init(&bars[i], (i == kBarPFull || i == kBarPFull + 1) ? static_cast<uint32_t>(kBM) : 1u);
+    *abort_flag = 0;
+    for (int i = 0; i < 6; ++i) counts[i] = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS[2] = {tmem, tmem + 2 * kBN};
+  const uint32_t tO[2] = {tmem + kBN, tmem + 3 * kBN};
+
+  if (warp == 0 && lane == 0) {
+    // ---- Q (both tiles) + K producer ----
+    prefetch_tensormap(&tmQ);
+    prefetch_tensormap(&tmK);
+    mbar_arrive_expect_tx(&bars[kBarQ], 2 * kTileBytes);
+    for (int x = 0; x < 2; ++x)
+      for (int h = 0; h < 2; ++h) {
+        const int t = q0 + x * kBM;  // rows past the prompt load as zeros and are never stored
+        const int c1 = p.q_tok_coord == 1 ? t : head, c2 = p.q_tok_coord == 1 ? head : t;
+        tma_load_3d(smem + (x ? kOffQB : kOffQA) + h * kHalf, &tmQ, &bars[kBarQ], h * 64, c1, c2);
+      }
+    for (int j = 0; j < n; ++j) {
+      const int s = j % kStages;
+      if (j >= kStages && !wait_bar(&bars[kBarKEmpty + s], ((j / kStages) - 1) & 1, abort_flag)) break;
+      mbar_arrive_expect_tx(&bars[kBarKFull + s], kTileBytes);
+      for (int h = 0; h < 2; ++h) {
+        const int t = j * kBN;
+        const int c1 = p.kv_tok_coord == 1 ? t : kvh, c2 = p.kv_tok_coord == 1 ? kvh : t;
+        tma_load_3d(smem + kOffK + s * kTileBytes + h * kHalf, &tmK, &bars[kBarKFull + s], h * 64,
+                    c1, c2);
+      }
+      counts[0] = j + 1;
+    }
+  } else if (warp == 2 && lane == 0) {
+    // ---- V producer ----
+    prefetch_tensormap(&tmV);
+    for (int j = 0; j < n; ++j) {
+      const int s = j % kStages;
+      if (j >= kStages && !wait_bar(&bars[kBarVEmpty + s], ((j / kStages) - 1) & 1, abort_flag)) break;
+      mbar_arrive_expect_tx(&bars[kBarVFull + s], kTileBytes);
+      for (int h = 0; h < 2; ++h) {
+        const int t = j * kBN;
+        const int c1 = p.kv_tok_coord == 1 ? t : kvh, c2 = p.kv_tok_coord == 1 ? kvh : t;
+        tma_load_3d(smem + kOffV + s * kTileBytes + h * kHalf, &tmV, &bars[kBarVFull + s], h * 64,
+                    c1, c2);
+      }
+      counts[1] = j + 1;
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    auto issue_qk = [&](int x, int j) {
+      const uint32_t qa = sbase + (x ? kOffQB : kOffQA);
+      const uint32_t kb = sbase + kOffK + (j % kStages) * kTileBytes;
+#pragma unroll
+      for (int k = 0; k < kHD / 16; ++k) {
+        const uint64_t da = smem_desc(qa + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+        const uint64_t db = smem_desc(kb + (k >> 2) * kHalf + (k & 3) * 32, 16, 1024);
+        mma_f16(tS[x], da, db, kIdescQK, k > 0 ? 1u : 0u);
+      }
+      mma_commit(&bars[kBarSFull + x]);
+      counts[2 + x] = j + 1;
+    };
+    auto issue_pv = [&](int x, int j) -> bool {
+      if (!wait_bar(&bars[kBarPFull + x], j & 1, abort_flag)) return false;
+      tc_fence_after();
+      const uint32_t vb = sbase + kOffV + (j % kStages) * kTileBytes;
+#pragma unroll
+      for (int k = 0; k < kBN / 16; ++k) {
+        const uint64_t db = smem_desc(vb + k * 2048, kHalf, 1024);
+        mma_f16_ts(tO[x], tS[x] + k * 8, db, kIdescPV, (j > 0 || k > 0) ? 1u : 0u);
+      }
+      mma_commit(&bars[kBarPVDone + x]);
+      counts[4 + x] = j + 1;
+      return true;
+    };
+    bool ok = wait_bar(&bars[kBarQ], 0, abort_flag);
+    if (ok && n > 0) {
+      ok = wait_bar(&bars[kBarKFull], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        if (n_t[0] > 0) issue_qk(0, 0);
+        if (n_t[1] > 0) issue_qk(1, 0);
+        mma_commit(&bars[kBarKEmpty]);
+      }
+    }
+    for (int j = 0; ok && j < n; ++j) {
+      const int s = j % kStages;
+      if (!wait_bar(&bars[kBarVFull + s], (j / kStages) & 1, abort_flag)) break;
+      tc_fence_after();
+      if (j < n_t[0] && !issue_pv(0, j)) break;
+      const bool next = j + 1 < n;
+      if (next) {
+        const int s1 = (j + 1) % kStages;
+        if (!wait_bar(&bars[kBarKFull + s1], ((j + 1) / kStages) & 1, abort_flag)) break;
+        tc_fence_after();
+      }
+      if (j + 1 < n_t[0]) issue_qk(0, j + 1);
+      if (j < n_t[1] && !issue_pv(1, j)) break;
+      mma_commit(&bars[kBarVEmpty + s]);
+      if (j + 1 < n_t[1]) issue_qk(1, j + 1);
+      if (next) mma_commit(&bars[kBarKEmpty + (j + 1) % kStages]);
+    }
+  } else if (warp >= 4) {
+    // ---- softmax: group x owns query tile x; thread r owns its whole 128-key row r ----
+    const int x = (warp - 4) >> 2;
+    const int r = (tid - 128) & 127;
+    const uint32_t lane_off = static_cast<uint32_t>(((warp - 4) & 3) * 32) << 16;
+    const int qi = q0 + x * kBM + r;
+    const int row_limit = offset + qi;
+    const int nx = n_t[x];
+    float m_used = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nx; ++j) {
+      if (!__all_sync(0xffffffffu, wait_bar(&bars[kBarSFull + x], j & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[128];
+      tmem_ld32(tS[x] + lane_off, *reinterpret_cast<float(*)[32]>(sv));
+      tmem_ld32(tS[x] + lane_off + 32, *reinterpret_cast<float(*)[32]>(sv + 32));
+      tmem_ld32(tS[x] + lane_off + 64, *reinterpret_cast<float(*)[32]>(sv + 64));
+      tmem_ld32(tS[x] + lane_off + 96, *reinterpret_cast<float(*)[32]>(sv + 96));
+      tmem_wait_ld();
+      const bool need_mask =
+          (p.causal && j * kBN + kBN - 1 > offset + q0 + x * kBM) || (j * kBN + kBN > p.kv_len);
+      if (need_mask) {
+        // keys j*128 + i with i >= nv are past the sequence or above the causal limit
+        const int lim = p.causal ? min(p.kv_len, row_limit + 1) : p.kv_len;
+        const int nv = lim - j * kBN;
+#pragma unroll
+        for (int i = 0; i < 128; ++i) sv[i] = i < nv ? sv[i] : -INFINITY;
+      }
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx8[i] = sv[i];
+#pragma unroll
+      for (int i = 8; i < 128; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+      const float row_max = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                  fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) *
+                            p.scale_log2;
+      const float m_new = fmaxf(m_used, row_max);
+      const bool grow = m_used == -INFINITY || m_new > m_used + kRescaleLog2;
+      const float alpha =
+          (grow && j > 0 && m_used != -INFINITY && m_new != -INFINITY) ? ex2(m_used - m_new) : 1.f;
+      if (grow) m_used = m_new;
+      const float ref = m_used == -INFINITY ? 0.f : m_used;
+      // P = 2^(s * scale_log2 - ref), written as packed bf16 over S in 8-column pieces (few live
+      // registers beside the 128 scores).
+      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+      const uint64_t nref2 = f2_pack(-ref, -ref);
+      uint64_t sum2[2] = {0ull, 0ull};
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int e = c * 16 + 2 * i;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(sv[e], sv[e + 1]), scale2, nref2), x0, x1);
+          const float a0 = ex2(x0), a1 = ex2(x1);
+          sum2[i & 1] = f2_add(sum2[i & 1], f2_pack(a0, a1));
+          pk[i] = pack_bf16x2(a0, a1);
+        }
+        tmem_st8u(tS[x] + lane_off + c * 8, pk);
+      }
+      {
+        float s0, s1;
+        f2_unpack(f2_add(sum2[0], sum2[1]), s0, s1);
+        l_sum = l_sum * alpha + (s0 + s1);
+      }
+      // Rescale O when the max grew past the threshold (rare after the first tiles); PV_x(j)
+      // cannot start before this group's P_x(j) arrival below, and PV_x(j-1) must have landed.
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        if (!__all_sync(0xffffffffu, wait_bar(&bars[kBarPVDone + x], (j - 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float v[32];
+          tmem_ld32(tO[x] + lane_off + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= alpha;
+          tmem_st32(tO[x] + lane_off + c * 32, v);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars[kBarPFull + x]);
+    }
+    if (ok && nx > 0 &&
+        __all_sync(0xffffffffu, wait_bar(&bars[kBarPVDone + x], (nx - 1) & 1, abort_flag))) {
+      tc_fence_after();
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      const bool write = qi < p.q_len;
+      bf16* orow = p.out + static_cast<int64_t>(qi) * p.o_st + static_cast<int64_t>(head) * p.o_sh;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tO[x] + lane_off + c * 32, v);
+        tmem_wait_ld();
+        if (write) {
+#pragma unroll
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 o4;
+            o4.x = pack_bf16x2(v[q8 * 8 + 0] * inv, v[q8 * 8 + 1] * inv);
+            o4.y = pack_bf16x2(v[q8 * 8 + 2] * inv, v[q8 * 8 + 3] * inv);
+            o4.z = pack_bf16x2(v[q8 * 8 + 4] * inv, v[q8 * 8 + 5] * inv);
+            o4.w = pack_bf16x2(v[q8 * 8 + 6] * inv, v[q8 * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + q8 * 8) = o4;
+          }
+        }
+      }
+    }
+  }
+
+  // ---- teardown ----
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag && tid == 0) {
+    const unsigned long long t0 = globaltimer_ns();
+    auto drain = [&](uint64_t* bar, uint32_t parity) {
+      while (!mbar_try_wait(smem_u32(bar), parity) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      }
+    };
+    drain(&bars[kBarQ], 0);
+    for (int t = max(0, counts[0] - kStages); t < counts[0]; ++t)
+      drain(&bars[kBarKFull + t % kStages], (t / kStages) & 1);
+    for (int t = max(0, counts[1] - kStages); t < counts[1]; ++t)
+      drain(&bars[kBarVFull + t % kStages], (t / kStages) & 1);
+    for (int x = 0; x < 2; ++x) {
+      if (counts[2 + x] > 0) drain(&bars[kBarSFull + x], (counts[2 + x] - 1) & 1);
+      if (counts[4 + x] > 0) drain(&bars[kBarPVDone + x], (counts[4 + x] - 1) & 1);
+    }
+  }
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols));
+  }
+}
+
+}  // namespace pp
+
 int build_map(CUtensorMap* map, const void* base, int64_t stride_tok, int64_t stride_head,
               int tokens, int heads, int* tok_coord) {
   if (stride_tok <= 0 || stride_head <= 0) return SOLORT_ERR_INVALID_ARGUMENT;
@@ -602,18 +949,28 @@ extern "C" int solort_attn_prefill(const SolortPrefillArgs* a, void* stream_v) {
   prm.q_tok_coord = q_tc;
   prm.kv_tok_coord = kv_tc;
   prm.scale_log2 = a->scale * 1.4426950408889634f;
-  const int64_t grid = static_cast<int64_t>(prm.q_tiles) * a->num_qo_heads;
+  // Long prompts: two query tiles per CTA in ping-pong (enough CTAs remain to fill the GPU).
+  const bool ping_pong = prm.q_tiles >= kPingPongMinTiles;
+  const int64_t grid = static_cast<int64_t>(ping_pong ? (prm.q_tiles + 1) / 2 : prm.q_tiles) *
+                       a->num_qo_heads;
   if (grid > (1ll << 31) - 1) return SOLORT_ERR_UNSUPPORTED;
+  if (ping_pong && di.max_smem_optin < pp::kSmemBytes) return SOLORT_ERR_UNSUPPORTED;
   static unsigned configured = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
   if (dev >= 32 || !(configured & (1u << dev))) {
     if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes) != cudaSuccess)
+                             kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(pp::prefill_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             pp::kSmemBytes) != cudaSuccess)
       return SOLORT_ERR_CUDA;
     if (dev < 32) configured |= 1u << dev;
   }
-  prefill_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes,
-                   static_cast<cudaStream_t>(stream_v)>>>(tq, tk, tv, prm);
+  if (ping_pong)
+    pp::prefill_pp_kernel<<<static_cast<unsigned>(grid), kThreads, pp::kSmemBytes,
+                            static_cast<cudaStream_t>(stream_v)>>>(tq, tk, tv, prm);
+  else
+    prefill_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes,
+                     static_cast<cudaStream_t>(stream_v)>>>(tq, tk, tv, prm);
   return launch_status();
 }

@@ -84,3 +84,28 @@ def test_prefill_golden_runner():
         v = torch.from_numpy(d[f"prefill.l{li}.v"]).to(torch.bfloat16).transpose(0, 1).contiguous()
         ref = torch.from_numpy(d[f"prefill.l{li}.out"]).transpose(0, 1)
         _close(ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda()), ref, f"golden prefill l{li}")
+
+
+# Prompts of 16 or more 128-row tiles take the two-tile ping-pong kernel.
+@pytest.mark.parametrize("T,nh,nkv", [(2048, 16, 8), (2049, 16, 8), (2300, 32, 8), (4096, 8, 8)])
+def test_prefill_ping_pong_causal(T, nh, nkv):
+    from solort_b200 import ops
+
+    q, k, v = A.make_attention_inputs(T * 3 + nh, nh, nkv, 128, T, T, 0)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, 0)
+    out = ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda())
+    torch.cuda.synchronize()
+    _close(out, ref, f"ping-pong prefill T={T} {nh}/{nkv}")
+    assert ops.device_status() == 0
+
+
+@pytest.mark.parametrize("q_len,kv_len,causal", [(2100, 3000, True), (2048, 2500, False)])
+def test_prefill_ping_pong_over_cache(q_len, kv_len, causal):
+    from solort_b200 import ops
+
+    q, k, v = A.make_attention_inputs(q_len + kv_len, 16, 8, 128, q_len, kv_len, kv_len - q_len)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, (kv_len - q_len) if causal else 10 ** 7)
+    out = ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+    torch.cuda.synchronize()
+    _close(out, ref, f"ping-pong q={q_len} kv={kv_len} causal={causal}")
+    assert ops.device_status() == 0
