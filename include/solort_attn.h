@@ -283,6 +283,42 @@ typedef struct SolortPrologueArgs {
 
 SOLORT_API int solort_attn_qk_norm_rope_append(const SolortPrologueArgs* args, void* stream);
 
+/*
+ * Layer glue of the runner's step (decode, verify or prefill) around the attention.
+ * solort_attn_add_rmsnorm: per row, x_out = x + delta (bf16, when delta != NULL; x_out may be x),
+ * then h_out = RMSNorm(x_out) * weight: fp32 x * rsqrt(mean(x^2) + eps), times the weight, cast to
+ * bf16 -- the reference's _rmsnorm (src/solort/model/cuda_graph_executor.py:25-28) after the
+ * layer loop's residual add; the fp32 sum of squares is a tree. hidden a multiple of 8 and at most
+ * 16384; pointers 16-byte aligned, strides (elements) multiples of 8.
+ * solort_attn_silu_mul: out[r, i] = bf16(bf16(silu(g)) * u) with g = gate_up[r, i] and
+ * u = gate_up[r, inter + i] -- the MLP's F.silu(gate) * up on the fused gate/up projection.
+ */
+typedef struct SolortAddRmsNormArgs {
+  const void* x;
+  int64_t x_stride;
+  const void* delta; /* optional */
+  int64_t delta_stride;
+  const void* weight;
+  void* x_out;
+  int64_t x_out_stride;
+  void* h_out;
+  int64_t h_out_stride;
+  int32_t rows, hidden;
+  float eps;
+} SolortAddRmsNormArgs;
+
+SOLORT_API int solort_attn_add_rmsnorm(const SolortAddRmsNormArgs* args, void* stream);
+
+typedef struct SolortSiluMulArgs {
+  const void* gate_up;
+  int64_t gate_up_stride;
+  void* out;
+  int64_t out_stride;
+  int32_t rows, inter;
+} SolortSiluMulArgs;
+
+SOLORT_API int solort_attn_silu_mul(const SolortSiluMulArgs* args, void* stream);
+
 /* Reads and clears the device status word of the current device (bit 0: an in-kernel wait hit
  * its time limit and the kernel returned without writing its output; bit 1: a tensor-memory
  * allocation wait hit its limit; bit 2: a kernel found its shared memory misaligned and returned

@@ -44,6 +44,8 @@ EXPORTED_SYMBOLS = (
     "solort_attn_exchange_buffer_close",
     "solort_attn_exchange_buffer_destroy",
     "solort_attn_qk_norm_rope_append",
+    "solort_attn_add_rmsnorm",
+    "solort_attn_silu_mul",
 )
 
 MAX_RANKS = 8  # SOLORT_MAX_RANKS
@@ -149,6 +151,30 @@ class SolortPrologueArgs(ctypes.Structure):
     ]
 
 
+class SolortAddRmsNormArgs(ctypes.Structure):
+    """Mirror of ``SolortAddRmsNormArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("x", c_vp), ("x_stride", c_i64),
+        ("delta", c_vp), ("delta_stride", c_i64),
+        ("weight", c_vp),
+        ("x_out", c_vp), ("x_out_stride", c_i64),
+        ("h_out", c_vp), ("h_out_stride", c_i64),
+        ("rows", c_i32), ("hidden", c_i32),
+        ("eps", c_f32),
+    ]
+
+
+class SolortSiluMulArgs(ctypes.Structure):
+    """Mirror of ``SolortSiluMulArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("gate_up", c_vp), ("gate_up_stride", c_i64),
+        ("out", c_vp), ("out_stride", c_i64),
+        ("rows", c_i32), ("inter", c_i32),
+    ]
+
+
 _LIB: ctypes.CDLL | None = None
 
 
@@ -203,6 +229,10 @@ def _optional_symbols(lib: ctypes.CDLL) -> None:
     lib.solort_attn_exchange_buffer_destroy.restype = ctypes.c_int
     lib.solort_attn_qk_norm_rope_append.argtypes = [P(SolortPrologueArgs), c_vp]
     lib.solort_attn_qk_norm_rope_append.restype = ctypes.c_int
+    lib.solort_attn_add_rmsnorm.argtypes = [P(SolortAddRmsNormArgs), c_vp]
+    lib.solort_attn_add_rmsnorm.restype = ctypes.c_int
+    lib.solort_attn_silu_mul.argtypes = [P(SolortSiluMulArgs), c_vp]
+    lib.solort_attn_silu_mul.restype = ctypes.c_int
 
 
 class SolortPrefillArgs(ctypes.Structure):

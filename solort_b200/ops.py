@@ -507,6 +507,60 @@ def qk_norm_rope_append(
     return q_out
 
 
+def add_rmsnorm(
+    x: torch.Tensor,
+    delta: torch.Tensor | None,
+    weight: torch.Tensor,
+    eps: float,
+    *,
+    x_out: torch.Tensor | None = None,
+    h_out: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """``x_out = x + delta`` (when ``delta`` is given; ``x_out`` may be ``x``) and
+    ``h_out = rmsnorm(x_out) * weight`` for ``[rows, hidden]`` bf16 rows, the reference's residual
+    add and ``_rmsnorm`` in one launch. Returns ``(x_out, h_out)`` (``x_out`` is ``x`` without a
+    delta)."""
+    _check_cuda("x", x, torch.bfloat16)
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise RuntimeError("x must be [rows, hidden] with contiguous rows")
+    rows, hidden = x.shape
+    if h_out is None:
+        h_out = torch.empty_like(x)
+    a = _lib.SolortAddRmsNormArgs()
+    a.x, a.x_stride = x.data_ptr(), x.stride(0)
+    if delta is not None:
+        _check_cuda("delta", delta, torch.bfloat16)
+        if x_out is None:
+            x_out = torch.empty_like(x)
+        a.delta, a.delta_stride = delta.data_ptr(), delta.stride(0)
+        a.x_out, a.x_out_stride = x_out.data_ptr(), x_out.stride(0)
+    else:
+        x_out = x
+    a.weight = weight.data_ptr()
+    a.h_out, a.h_out_stride = h_out.data_ptr(), h_out.stride(0)
+    a.rows, a.hidden, a.eps = rows, hidden, float(eps)
+    _lib.check(_lib.load().solort_attn_add_rmsnorm(ctypes.byref(a), ctypes.c_void_p(_stream(x.device))),
+               "solort_attn_add_rmsnorm")
+    return x_out, h_out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``silu(gate) * up`` of a fused ``[rows, 2 * inter]`` gate/up projection (bf16)."""
+    _check_cuda("gate_up", gate_up, torch.bfloat16)
+    if gate_up.dim() != 2 or gate_up.stride(1) != 1 or gate_up.shape[1] % 2:
+        raise RuntimeError("gate_up must be [rows, 2 * inter] with contiguous rows")
+    rows, inter = gate_up.shape[0], gate_up.shape[1] // 2
+    if out is None:
+        out = torch.empty(rows, inter, dtype=torch.bfloat16, device=gate_up.device)
+    a = _lib.SolortSiluMulArgs()
+    a.gate_up, a.gate_up_stride = gate_up.data_ptr(), gate_up.stride(0)
+    a.out, a.out_stride = out.data_ptr(), out.stride(0)
+    a.rows, a.inter = rows, inter
+    _lib.check(_lib.load().solort_attn_silu_mul(ctypes.byref(a), ctypes.c_void_p(_stream(gate_up.device))),
+               "solort_attn_silu_mul")
+    return out
+
+
 def device_status() -> int:
     """Read and clear the library's device status word (nonzero: an in-kernel wait timed out)."""
     flags = ctypes.c_uint(0)

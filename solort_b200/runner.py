@@ -15,9 +15,10 @@ What changes is the attention at the three inline sites:
   ``ops.gqa_decode`` with ``q_len = K + 1`` (per-row causal limit, no expansion).
 With ``prologue="fused"`` (the default) the per-head QK-RMSNorm, RoPE and KV append of each
 layer (``:176-179, 120-123, 257-260``) run as one ``ops.qk_norm_rope_append`` launch reading the
-model's bf16 cos/sin tables; ``prologue="torch"`` keeps the reference's torch ops there.
-Everything else (weights fusion, input / post norms, MLP, lm_head, argmax) is the same math as the
-reference.
+model's bf16 cos/sin tables; with ``glue="fused"`` (the default) each residual add and the RMSNorm
+after it run as one ``ops.add_rmsnorm`` launch and F.silu(gate) * up as one ``ops.silu_mul``;
+``"torch"`` keeps the reference's torch ops at either place. The projections, lm_head and argmax
+are the reference's torch calls.
 """
 
 from __future__ import annotations
@@ -37,10 +38,10 @@ def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 class GraphQwen3Runner:
     MAX_VERIFY_TOKENS = 8
 
-    def __init__(self, model, max_len: int, prologue: str = "fused") -> None:
-        if prologue not in ("fused", "torch"):
-            raise ValueError(prologue)
-        self.prologue = prologue
+    def __init__(self, model, max_len: int, prologue: str = "fused", glue: str = "fused") -> None:
+        if prologue not in ("fused", "torch") or glue not in ("fused", "torch"):
+            raise ValueError((prologue, glue))
+        self.prologue, self.glue = prologue, glue
         c = model.config
         self.dev = next(model.parameters()).device
         if self.dev.type != "cuda":
@@ -112,8 +113,7 @@ class GraphQwen3Runner:
         d = x.shape[-1] // 2
         return x * cos + torch.cat([-x[..., d:], x[..., :d]], -1) * sin
 
-    def _qkv(self, x: torch.Tensor, ly: dict, t: int, cos, sin):
-        h = _rmsnorm(x, ly["in_ln"], self.eps)
+    def _qkv(self, h: torch.Tensor, ly: dict, t: int, cos, sin):
         q, k, v = (h @ ly["wqkv"].T).split([self.q_dim, self.kv_dim, self.kv_dim], dim=-1)
         q = q.view(t, self.nh, self.hd).transpose(0, 1)
         k = k.view(t, self.nkv, self.hd).transpose(0, 1)
@@ -122,17 +122,17 @@ class GraphQwen3Runner:
         k = self._rope(_rmsnorm(k, ly["kn"], self.eps), cos, sin)
         return q, k, v  # [heads, t, hd]
 
-    def _attn_inputs(self, x: torch.Tensor, ly: dict, li: int, t: int, pos_t: torch.Tensor,
+    def _attn_inputs(self, h: torch.Tensor, ly: dict, li: int, t: int, pos_t: torch.Tensor,
                      pos_rows: torch.Tensor, cos, sin) -> torch.Tensor:
-        """Queries ``[t, nh, hd]`` of layer ``li`` for tokens at ``pos_t[0] ..``, with the tokens' K / V
-        appended to ``kc[li]``/``vc[li]`` (``pos_rows``: the same positions as a vector)."""
+        """Queries ``[t, nh, hd]`` of layer ``li`` from its normed input ``h`` for tokens at
+        ``pos_t[0] ..``, with the tokens' K / V appended to ``kc[li]``/``vc[li]`` (``pos_rows``: the
+        same positions as a vector)."""
         if self.prologue == "fused":
-            h = _rmsnorm(x, ly["in_ln"], self.eps)
             qkv = h @ ly["wqkv"].T
             return ops.qk_norm_rope_append(qkv, ly["qn"], ly["kn"], self.eps, self.cos_tab,
                                            self.sin_tab, pos_t, self.kc[li], self.vc[li],
                                            num_qo_heads=self.nh, num_kv_heads=self.nkv)
-        q, k, v = self._qkv(x, ly, t, cos, sin)
+        q, k, v = self._qkv(h, ly, t, cos, sin)
         self.kc[li].index_copy_(0, pos_rows, k.transpose(0, 1))
         self.vc[li].index_copy_(0, pos_rows, v.transpose(0, 1))
         return q.transpose(0, 1)
@@ -142,18 +142,39 @@ class GraphQwen3Runner:
         gate, up = (h2 @ ly["wgu"].T).split([self.inter, self.inter], dim=-1)
         return x + (F.silu(gate) * up) @ ly["wd"].T
 
+    def _layer_stack(self, x: torch.Tensor, t: int, pos_t: torch.Tensor, pos_rows: torch.Tensor,
+                     cos, sin, attend) -> torch.Tensor:
+        """The decoder layers over hidden states ``x [t, hidden]`` (updated in place with the fused
+        glue), ``attend(li, q [t, nh, hd]) -> ctx``; returns the final-normed states. The fused glue
+        folds each residual add into the next RMSNorm and SiLU(gate) * up into one launch."""
+        if self.glue == "fused":
+            _, h = ops.add_rmsnorm(x, None, self.layers[0]["in_ln"], self.eps)
+            for li, ly in enumerate(self.layers):
+                q = self._attn_inputs(h, ly, li, t, pos_t, pos_rows, cos, sin)
+                o = attend(li, q).reshape(t, self.q_dim) @ ly["wo"].T
+                _, h2 = ops.add_rmsnorm(x, o, ly["post_ln"], self.eps, x_out=x)
+                dn = ops.silu_mul(h2 @ ly["wgu"].T) @ ly["wd"].T
+                nxt = self.layers[li + 1]["in_ln"] if li + 1 < self.L else self.final_norm
+                _, h = ops.add_rmsnorm(x, dn, nxt, self.eps, x_out=x)
+            return h
+        for li, ly in enumerate(self.layers):
+            q = self._attn_inputs(_rmsnorm(x, ly["in_ln"], self.eps), ly, li, t, pos_t, pos_rows,
+                                  cos, sin)
+            x = x + attend(li, q).reshape(t, self.q_dim) @ ly["wo"].T
+            x = self._mlp(x, ly)
+        return _rmsnorm(x, self.final_norm, self.eps)
+
     # ---- prefill ----
     def _prefill_forward(self, bound: int) -> torch.Tensor:
         t = bound
         rows = torch.arange(t, device=self.dev)
         cos, sin = (None, None) if self.prologue == "fused" else self._cos_sin(rows)
-        x = self.embed[self.pre_tok[:bound]].to(self.dt)
-        for li, ly in enumerate(self.layers):
-            q = self._attn_inputs(x, ly, li, t, self.zero_pos, rows, cos, sin)  # [t, nh, hd]
-            ctx = ops.gqa_prefill(q, self.kc[li, :t], self.vc[li, :t], causal=True, scale=self.scale)
-            x = x + ctx.reshape(t, self.q_dim) @ ly["wo"].T
-            x = self._mlp(x, ly)
-        return _rmsnorm(x, self.final_norm, self.eps)
+        x = self.embed[self.pre_tok[:bound]].to(self.dt).contiguous()
+
+        def attend(li, q):
+            return ops.gqa_prefill(q, self.kc[li, :t], self.vc[li, :t], causal=True, scale=self.scale)
+
+        return self._layer_stack(x, t, self.zero_pos, rows, cos, sin, attend)
 
     def _capture_prefill(self, bound: int) -> None:
         stream = torch.cuda.Stream()
@@ -180,15 +201,14 @@ class GraphQwen3Runner:
     # ---- decode ----
     def _decode_forward(self, bound: int) -> torch.Tensor:
         cos, sin = (None, None) if self.prologue == "fused" else self._cos_sin(self.pos_buf)
-        x = self.embed[self.tok_buf].to(self.dt)
-        for li, ly in enumerate(self.layers):
-            q = self._attn_inputs(x, ly, li, 1, self.pos_buf, self.pos_buf, cos, sin)
-            ctx = ops.gqa_decode(q.reshape(1, 1, self.nh, self.hd), self.kc[li], self.vc[li],
-                                 self.pos_buf, scale=self.scale, max_kv_len=bound,
-                                 workspace=self.attn_ws)
-            x = x + ctx.reshape(1, self.q_dim) @ ly["wo"].T
-            x = self._mlp(x, ly)
-        x = _rmsnorm(x, self.final_norm, self.eps)
+        x = self.embed[self.tok_buf].to(self.dt).contiguous()
+
+        def attend(li, q):
+            return ops.gqa_decode(q.reshape(1, 1, self.nh, self.hd), self.kc[li], self.vc[li],
+                                  self.pos_buf, scale=self.scale, max_kv_len=bound,
+                                  workspace=self.attn_ws)
+
+        x = self._layer_stack(x, 1, self.pos_buf, self.pos_buf, cos, sin, attend)
         return (x @ self.lm_head.T).float()
 
     def _bucket_for(self, pos: int) -> int:
@@ -242,14 +262,14 @@ class GraphQwen3Runner:
         k1 = self.vtok.shape[0]
         pos = self.vpos0 + torch.arange(k1, device=self.dev)
         cos, sin = (None, None) if self.prologue == "fused" else self._cos_sin(pos)
-        x = self.embed[self.vtok].to(self.dt)
-        for li, ly in enumerate(self.layers):
-            q = self._attn_inputs(x, ly, li, k1, self.vpos0, pos, cos, sin)
-            ctx = ops.gqa_decode(q.reshape(1, k1, self.nh, self.hd), self.kc[li],
-                                 self.vc[li], self.vpos0, scale=self.scale, workspace=self.attn_ws)
-            x = x + ctx.reshape(k1, self.q_dim) @ ly["wo"].T
-            x = self._mlp(x, ly)
-        return (_rmsnorm(x, self.final_norm, self.eps) @ self.lm_head.T).float()
+        x = self.embed[self.vtok].to(self.dt).contiguous()
+
+        def attend(li, q):
+            return ops.gqa_decode(q.reshape(1, k1, self.nh, self.hd), self.kc[li], self.vc[li],
+                                  self.vpos0, scale=self.scale, workspace=self.attn_ws)
+
+        x = self._layer_stack(x, k1, self.vpos0, pos, cos, sin, attend)
+        return (x @ self.lm_head.T).float()
 
     def verify(self, tok_t: torch.Tensor, pos_start: int) -> torch.Tensor:
         if self.verify_graph is None:

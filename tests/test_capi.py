@@ -68,7 +68,9 @@ def _c_layout(struct: str, fields: list[str]) -> dict[str, int]:
 STRUCTS = [(_lib.SolortDecodeArgs, "SolortDecodeArgs"), (_lib.SolortMergeArgs, "SolortMergeArgs"),
            (_lib.SolortExchangeArgs, "SolortExchangeArgs"),
            (_lib.SolortExchangeMergeArgs, "SolortExchangeMergeArgs"),
-           (_lib.SolortPrologueArgs, "SolortPrologueArgs")]
+           (_lib.SolortPrologueArgs, "SolortPrologueArgs"),
+           (_lib.SolortAddRmsNormArgs, "SolortAddRmsNormArgs"),
+           (_lib.SolortSiluMulArgs, "SolortSiluMulArgs")]
 
 
 @pytest.mark.parametrize("cls,name", STRUCTS + ([(_lib.SolortPrefillArgs, "SolortPrefillArgs")]
