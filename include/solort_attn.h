@@ -319,6 +319,40 @@ typedef struct SolortSiluMulArgs {
 
 SOLORT_API int solort_attn_silu_mul(const SolortSiluMulArgs* args, void* stream);
 
+/*
+ * Weight-streaming projection for the decode step (t <= 8 token rows), replacing the runner's
+ * torch matmuls against a bf16 Linear weight W [n, k] (row stride w_stride):
+ *   y[r, j] = bf16( sum_i act[r, i] * W[j, i] )   (fp32 accumulation)
+ * mode 0: act = a [t, k];
+ * mode 1: act = bf16(bf16(silu(g)) * u) with g = a[r, 0:k], u = a[r, k:2k] (the MLP's
+ *         F.silu(gate) * up fused into the down projection);
+ * mode 2: act = RMSNorm(x) * norm_weight with x = a (the residual stream) or, when delta is given,
+ *         x = bf16(a + delta), which is also written to x_out (the residual add and the norm after
+ *         it, bit-identical to solort_attn_add_rmsnorm); x_out must not overlap a or delta.
+ * W is read before the kernel waits for the previous kernel on the stream (PDL), so it must not be
+ * written by that kernel. k a multiple of 8, t * k * 2 bytes staged per CTA at most 160 KB;
+ * pointers 16-byte aligned, strides multiples of 8 elements.
+ * Reference: src/solort/model/cuda_graph_executor.py _rmsnorm :25-28 and the layer loop's
+ * projections (:168-190).
+ */
+typedef struct SolortGemvArgs {
+  const void* a;
+  int64_t a_stride;
+  const void* w;
+  int64_t w_stride;
+  void* y;
+  int64_t y_stride;
+  int32_t t, n, k, mode;
+  const void* delta;        /* mode 2, optional */
+  int64_t delta_stride;
+  const void* norm_weight;  /* mode 2: [k] */
+  void* x_out;              /* mode 2 with delta */
+  int64_t x_out_stride;
+  float eps;
+} SolortGemvArgs;
+
+SOLORT_API int solort_attn_gemv(const SolortGemvArgs* args, void* stream);
+
 /* Reads and clears the device status word of the current device (bit 0: an in-kernel wait hit
  * its time limit and the kernel returned without writing its output; bit 1: a tensor-memory
  * allocation wait hit its limit; bit 2: a kernel found its shared memory misaligned and returned

@@ -46,6 +46,7 @@ EXPORTED_SYMBOLS = (
     "solort_attn_qk_norm_rope_append",
     "solort_attn_add_rmsnorm",
     "solort_attn_silu_mul",
+    "solort_attn_gemv",
 )
 
 MAX_RANKS = 8  # SOLORT_MAX_RANKS
@@ -175,6 +176,21 @@ class SolortSiluMulArgs(ctypes.Structure):
     ]
 
 
+class SolortGemvArgs(ctypes.Structure):
+    """Mirror of ``SolortGemvArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("a", c_vp), ("a_stride", c_i64),
+        ("w", c_vp), ("w_stride", c_i64),
+        ("y", c_vp), ("y_stride", c_i64),
+        ("t", c_i32), ("n", c_i32), ("k", c_i32), ("mode", c_i32),
+        ("delta", c_vp), ("delta_stride", c_i64),
+        ("norm_weight", c_vp),
+        ("x_out", c_vp), ("x_out_stride", c_i64),
+        ("eps", ctypes.c_float),
+    ]
+
+
 _LIB: ctypes.CDLL | None = None
 
 
@@ -233,6 +249,8 @@ def _optional_symbols(lib: ctypes.CDLL) -> None:
     lib.solort_attn_add_rmsnorm.restype = ctypes.c_int
     lib.solort_attn_silu_mul.argtypes = [P(SolortSiluMulArgs), c_vp]
     lib.solort_attn_silu_mul.restype = ctypes.c_int
+    lib.solort_attn_gemv.argtypes = [P(SolortGemvArgs), c_vp]
+    lib.solort_attn_gemv.restype = ctypes.c_int
 
 
 class SolortPrefillArgs(ctypes.Structure):

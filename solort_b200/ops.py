@@ -561,6 +561,53 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     return out
 
 
+def gemv(a: torch.Tensor, weight: torch.Tensor, *, silu_gate_up: bool = False,
+         out: torch.Tensor | None = None, norm_weight: torch.Tensor | None = None,
+         delta: torch.Tensor | None = None, x_out: torch.Tensor | None = None,
+         eps: float = 1e-6) -> torch.Tensor:
+    """``act @ weight[n, k].T`` for ``t <= 8`` token rows as a weight stream (bf16 out, fp32
+    accumulation). ``act`` is ``a [t, k]``; with ``silu_gate_up``, ``silu(gate) * up`` of a fused
+    ``[t, 2k]`` gate/up projection ``a``; with ``norm_weight``, ``RMSNorm(x) * norm_weight`` of the
+    residual stream ``x = a`` or, given ``delta``, of ``x = a + delta``, which is then also written
+    to ``x_out`` (a separate buffer; the residual add and norm of the layer loop, bit-identical to
+    :func:`add_rmsnorm`)."""
+    _check_cuda("a", a, torch.bfloat16)
+    _check_cuda("weight", weight, torch.bfloat16)
+    if a.dim() != 2 or a.stride(1) != 1 or weight.dim() != 2 or weight.stride(1) != 1:
+        raise RuntimeError("a and weight must be 2-D with contiguous rows")
+    t = a.shape[0]
+    n, k = weight.shape
+    if silu_gate_up and norm_weight is not None:
+        raise RuntimeError("silu_gate_up and norm_weight are exclusive")
+    if a.shape[1] != (2 * k if silu_gate_up else k):
+        raise RuntimeError(f"a has {a.shape[1]} columns for a weight with k={k}")
+    if out is None:
+        out = torch.empty(t, n, dtype=torch.bfloat16, device=a.device)
+    g = _lib.SolortGemvArgs()
+    g.a, g.a_stride = a.data_ptr(), a.stride(0)
+    g.w, g.w_stride = weight.data_ptr(), weight.stride(0)
+    g.y, g.y_stride = out.data_ptr(), out.stride(0)
+    g.t, g.n, g.k, g.mode = t, n, k, 1 if silu_gate_up else 0
+    if norm_weight is not None:
+        _check_cuda("norm_weight", norm_weight, torch.bfloat16)
+        if norm_weight.shape != (k,) or not norm_weight.is_contiguous():
+            raise RuntimeError(f"norm_weight must be a contiguous [{k}] vector")
+        g.mode, g.norm_weight, g.eps = 2, norm_weight.data_ptr(), float(eps)
+        if delta is not None:
+            _check_cuda("delta", delta, torch.bfloat16)
+            if x_out is None:
+                raise RuntimeError("delta needs x_out (the updated residual stream)")
+            _check_cuda("x_out", x_out, torch.bfloat16)
+            for name, ten in (("delta", delta), ("x_out", x_out)):
+                if ten.shape != a.shape or ten.stride(1) != 1:
+                    raise RuntimeError(f"{name} must be [{t}, {k}] with contiguous rows")
+            g.delta, g.delta_stride = delta.data_ptr(), delta.stride(0)
+            g.x_out, g.x_out_stride = x_out.data_ptr(), x_out.stride(0)
+    _lib.check(_lib.load().solort_attn_gemv(ctypes.byref(g), ctypes.c_void_p(_stream(a.device))),
+               "solort_attn_gemv")
+    return out
+
+
 def device_status() -> int:
     """Read and clear the library's device status word (nonzero: an in-kernel wait timed out)."""
     flags = ctypes.c_uint(0)

@@ -17,8 +17,14 @@ With ``prologue="fused"`` (the default) the per-head QK-RMSNorm, RoPE and KV app
 layer (``:176-179, 120-123, 257-260``) run as one ``ops.qk_norm_rope_append`` launch reading the
 model's bf16 cos/sin tables; with ``glue="fused"`` (the default) each residual add and the RMSNorm
 after it run as one ``ops.add_rmsnorm`` launch and F.silu(gate) * up as one ``ops.silu_mul``;
-``"torch"`` keeps the reference's torch ops at either place. The projections, lm_head and argmax
-are the reference's torch calls.
+``"torch"`` keeps the reference's torch ops at either place. With ``proj="gemv"`` (the default)
+the decode step's projections and lm_head (one token row, where a weight stream beats cuBLAS) run
+as ``ops.gemv`` launches that also carry the layer glue: each residual add + RMSNorm runs in the
+staging of the projection after it (qkv, gate_up, lm_head) and SiLU(gate) * up in the down
+projection's, so a decoder layer is six launches (qkv, prologue, attention, o, gate_up, down;
+plus the split-KV merge when the attention splits). The residual stream alternates between two
+buffers because the fused norm writes x + delta while other CTAs still read x. Verify's K + 1 rows,
+prefill's projections and the argmax use the reference's torch calls.
 """
 
 from __future__ import annotations
@@ -37,11 +43,14 @@ def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 class GraphQwen3Runner:
     MAX_VERIFY_TOKENS = 8
+    GEMV_MAX_ROWS = 1  # weight-streaming projections for one token row; cuBLAS from two rows on
 
-    def __init__(self, model, max_len: int, prologue: str = "fused", glue: str = "fused") -> None:
-        if prologue not in ("fused", "torch") or glue not in ("fused", "torch"):
-            raise ValueError((prologue, glue))
-        self.prologue, self.glue = prologue, glue
+    def __init__(self, model, max_len: int, prologue: str = "fused", glue: str = "fused",
+                 proj: str = "gemv") -> None:
+        if prologue not in ("fused", "torch") or glue not in ("fused", "torch") or \
+                proj not in ("gemv", "torch"):
+            raise ValueError((prologue, glue, proj))
+        self.prologue, self.glue, self.proj = prologue, glue, proj
         c = model.config
         self.dev = next(model.parameters()).device
         if self.dev.type != "cuda":
@@ -122,13 +131,26 @@ class GraphQwen3Runner:
         k = self._rope(_rmsnorm(k, ly["kn"], self.eps), cos, sin)
         return q, k, v  # [heads, t, hd]
 
+    def _mm(self, a: torch.Tensor, w: torch.Tensor, silu_gate_up: bool = False) -> torch.Tensor:
+        """``act(a) @ w.T``: the weight-streaming kernel for the decode / verify step's few rows
+        (``proj="gemv"``), the torch matmul otherwise (prefill's GEMM-shaped calls)."""
+        if self.proj == "gemv" and a.shape[0] <= self.GEMV_MAX_ROWS:
+            return ops.gemv(a, w, silu_gate_up=silu_gate_up)
+        if silu_gate_up:
+            a = ops.silu_mul(a) if self.glue == "fused" else self._silu_up(a)
+        return a @ w.T
+
+    def _silu_up(self, gu: torch.Tensor) -> torch.Tensor:
+        gate, up = gu.split([self.inter, self.inter], dim=-1)
+        return F.silu(gate) * up
+
     def _attn_inputs(self, h: torch.Tensor, ly: dict, li: int, t: int, pos_t: torch.Tensor,
                      pos_rows: torch.Tensor, cos, sin) -> torch.Tensor:
         """Queries ``[t, nh, hd]`` of layer ``li`` from its normed input ``h`` for tokens at
         ``pos_t[0] ..``, with the tokens' K / V appended to ``kc[li]``/``vc[li]`` (``pos_rows``: the
         same positions as a vector)."""
         if self.prologue == "fused":
-            qkv = h @ ly["wqkv"].T
+            qkv = self._mm(h, ly["wqkv"])
             return ops.qk_norm_rope_append(qkv, ly["qn"], ly["kn"], self.eps, self.cos_tab,
                                            self.sin_tab, pos_t, self.kc[li], self.vc[li],
                                            num_qo_heads=self.nh, num_kv_heads=self.nkv)
@@ -143,26 +165,61 @@ class GraphQwen3Runner:
         return x + (F.silu(gate) * up) @ ly["wd"].T
 
     def _layer_stack(self, x: torch.Tensor, t: int, pos_t: torch.Tensor, pos_rows: torch.Tensor,
-                     cos, sin, attend) -> torch.Tensor:
+                     cos, sin, attend, lm_head: bool = False) -> torch.Tensor:
         """The decoder layers over hidden states ``x [t, hidden]`` (updated in place with the fused
-        glue), ``attend(li, q [t, nh, hd]) -> ctx``; returns the final-normed states. The fused glue
-        folds each residual add into the next RMSNorm and SiLU(gate) * up into one launch."""
+        glue), ``attend(li, q [t, nh, hd]) -> ctx``; returns the final-normed states, or with
+        ``lm_head`` the logits. The fused glue folds each residual add into the next RMSNorm and
+        SiLU(gate) * up into one launch; with one token row both ride inside the projections."""
+        if (self.glue == "fused" and self.prologue == "fused" and self.proj == "gemv"
+                and t <= self.GEMV_MAX_ROWS):
+            return self._streamed_stack(x, t, pos_t, attend, lm_head)
         if self.glue == "fused":
             _, h = ops.add_rmsnorm(x, None, self.layers[0]["in_ln"], self.eps)
             for li, ly in enumerate(self.layers):
                 q = self._attn_inputs(h, ly, li, t, pos_t, pos_rows, cos, sin)
-                o = attend(li, q).reshape(t, self.q_dim) @ ly["wo"].T
+                o = self._mm(attend(li, q).reshape(t, self.q_dim), ly["wo"])
                 _, h2 = ops.add_rmsnorm(x, o, ly["post_ln"], self.eps, x_out=x)
-                dn = ops.silu_mul(h2 @ ly["wgu"].T) @ ly["wd"].T
+                dn = self._mm(self._mm(h2, ly["wgu"]), ly["wd"], silu_gate_up=True)
                 nxt = self.layers[li + 1]["in_ln"] if li + 1 < self.L else self.final_norm
                 _, h = ops.add_rmsnorm(x, dn, nxt, self.eps, x_out=x)
-            return h
+        else:
+            for li, ly in enumerate(self.layers):
+                q = self._attn_inputs(_rmsnorm(x, ly["in_ln"], self.eps), ly, li, t, pos_t,
+                                      pos_rows, cos, sin)
+                x = x + attend(li, q).reshape(t, self.q_dim) @ ly["wo"].T
+                x = self._mlp(x, ly)
+            h = _rmsnorm(x, self.final_norm, self.eps)
+        return self._mm(h, self.lm_head) if lm_head else h
+
+    def _streamed_stack(self, x: torch.Tensor, t: int, pos_t: torch.Tensor, attend,
+                        lm_head: bool) -> torch.Tensor:
+        """One-token-row decoder layers as weight streams with the glue inside: x + delta and its
+        RMSNorm in the qkv / gate_up / lm_head staging, SiLU(gate) * up in the down projection."""
+        xs = (x, torch.empty_like(x))
+        cur, delta, norm = 0, None, self.layers[0]["in_ln"]
+
+        def normed_proj(w, nw):
+            nonlocal cur
+            if delta is None:
+                return ops.gemv(xs[cur], w, norm_weight=nw, eps=self.eps)
+            y = ops.gemv(xs[cur], w, norm_weight=nw, delta=delta, x_out=xs[1 - cur], eps=self.eps)
+            cur = 1 - cur
+            return y
+
         for li, ly in enumerate(self.layers):
-            q = self._attn_inputs(_rmsnorm(x, ly["in_ln"], self.eps), ly, li, t, pos_t, pos_rows,
-                                  cos, sin)
-            x = x + attend(li, q).reshape(t, self.q_dim) @ ly["wo"].T
-            x = self._mlp(x, ly)
-        return _rmsnorm(x, self.final_norm, self.eps)
+            qkv = normed_proj(ly["wqkv"], norm)
+            q = ops.qk_norm_rope_append(qkv, ly["qn"], ly["kn"], self.eps, self.cos_tab,
+                                        self.sin_tab, pos_t, self.kc[li], self.vc[li],
+                                        num_qo_heads=self.nh, num_kv_heads=self.nkv)
+            delta = ops.gemv(attend(li, q).reshape(t, self.q_dim), ly["wo"])
+            gu = normed_proj(ly["wgu"], ly["post_ln"])
+            delta = ops.gemv(gu, ly["wd"], silu_gate_up=True)
+            norm = self.layers[li + 1]["in_ln"] if li + 1 < self.L else self.final_norm
+        if lm_head:
+            return normed_proj(self.lm_head, self.final_norm)
+        _, h = ops.add_rmsnorm(xs[cur], delta, self.final_norm, self.eps,
+                               x_out=xs[1 - cur])
+        return h
 
     # ---- prefill ----
     def _prefill_forward(self, bound: int) -> torch.Tensor:
@@ -196,7 +253,7 @@ class GraphQwen3Runner:
         if bound not in self._pre_graphs:
             self._capture_prefill(bound)
         self._pre_graphs[bound].replay()
-        return (self._pre_hidden[bound][plen - 1: plen] @ self.lm_head.T).float()
+        return self._mm(self._pre_hidden[bound][plen - 1: plen], self.lm_head).float()
 
     # ---- decode ----
     def _decode_forward(self, bound: int) -> torch.Tensor:
@@ -208,8 +265,8 @@ class GraphQwen3Runner:
                                   self.pos_buf, scale=self.scale, max_kv_len=bound,
                                   workspace=self.attn_ws)
 
-        x = self._layer_stack(x, 1, self.pos_buf, self.pos_buf, cos, sin, attend)
-        return (x @ self.lm_head.T).float()
+        return self._layer_stack(x, 1, self.pos_buf, self.pos_buf, cos, sin, attend,
+                                 lm_head=True).float()
 
     def _bucket_for(self, pos: int) -> int:
         return next(b for b in self.buckets if b > pos)
@@ -268,8 +325,7 @@ class GraphQwen3Runner:
             return ops.gqa_decode(q.reshape(1, k1, self.nh, self.hd), self.kc[li], self.vc[li],
                                   self.vpos0, scale=self.scale, workspace=self.attn_ws)
 
-        x = self._layer_stack(x, k1, self.vpos0, pos, cos, sin, attend)
-        return (x @ self.lm_head.T).float()
+        return self._layer_stack(x, k1, self.vpos0, pos, cos, sin, attend, lm_head=True).float()
 
     def verify(self, tok_t: torch.Tensor, pos_start: int) -> torch.Tensor:
         if self.verify_graph is None:

@@ -70,7 +70,8 @@ STRUCTS = [(_lib.SolortDecodeArgs, "SolortDecodeArgs"), (_lib.SolortMergeArgs, "
            (_lib.SolortExchangeMergeArgs, "SolortExchangeMergeArgs"),
            (_lib.SolortPrologueArgs, "SolortPrologueArgs"),
            (_lib.SolortAddRmsNormArgs, "SolortAddRmsNormArgs"),
-           (_lib.SolortSiluMulArgs, "SolortSiluMulArgs")]
+           (_lib.SolortSiluMulArgs, "SolortSiluMulArgs"),
+           (_lib.SolortGemvArgs, "SolortGemvArgs")]
 
 
 @pytest.mark.parametrize("cls,name", STRUCTS + ([(_lib.SolortPrefillArgs, "SolortPrefillArgs")]
