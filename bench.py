@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: partials cross GPUs by NVLink peer stores (p2p) or an NCCL all-gather")
     ap.add_argument("--prefill-T", type=int, nargs="+", default=[512, 1024, 4096])
+    ap.add_argument("--no-stable-prefix", action="store_true",
+                    help="decode calls without SOLORT_DECODE_STABLE_PREFIX (keys requested only "
+                         "after the previous kernel finished)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the paged / long-context / tok/s sections of the default line")
     return ap.parse_args()
@@ -249,13 +252,18 @@ def run_gpu_arm(args) -> None:
         sharded = ShardedDecode(rank, world, num_qo_heads=NH, layers=LAYERS, device=dev,
                                 exchange=args.exchange)
 
+    # q_pos and every key are written before the graph: the calls may request their keys while
+    # the previous layer's kernels finish (SOLORT_DECODE_STABLE_PREFIX), as the runner's do.
+    stable = not args.no_stable_prefix
+
     def step():
         for li in range(LAYERS):
             if sharded is None:
                 ops.gqa_decode(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND",
-                               out=outs[li], workspace=ws)
+                               out=outs[li], workspace=ws, stable_prefix=stable)
             else:
-                sharded.layer(li, q[li], kv[li, 0], kv[li, 1], qpos, rank * ctx, outs[li], ws)
+                sharded.layer(li, q[li], kv[li, 0], kv[li, 1], qpos, rank * ctx, outs[li], ws,
+                              stable_prefix=stable)
 
     # capture one step in a graph (side-stream warm-up first, as the reference does)
     s = torch.cuda.Stream(device=dev)
@@ -309,10 +317,12 @@ def run_gpu_arm(args) -> None:
     calls = []
     if sharded is None:
         calls = [ops.DecodeCall(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND",
-                                out=outs[li], workspace=ws) for li in range(LAYERS)]
+                                out=outs[li], workspace=ws, stable_prefix=stable)
+                 for li in range(LAYERS)]
     elif args.exchange == "p2p":
         calls = [sharded.prepared_layer(li, q[li], kv[li, 0], kv[li, 1], qpos, rank * ctx,
-                                        outs[li], ws) for li in range(LAYERS)]
+                                        outs[li], ws, stable_prefix=stable)
+                 for li in range(LAYERS)]
 
     def e2e_step():
         q.copy_(q_host, non_blocking=True)
@@ -376,6 +386,7 @@ def run_gpu_arm(args) -> None:
                           else "NCCL all_gather_into_tensor + lse_merge") if world > 1 else None),
             "l2": "inputs larger than L2: 36 layers x 32 MiB KV per GPU replayed in order",
             "graph": "36 layer calls per CUDA graph replay",
+            "stable_prefix": stable,
         },
         "pct_of_8TBs": round(100 * value / world / 8000, 2),
         "roofline": {
@@ -459,7 +470,7 @@ def _sweep(kv, q, qpos_full, ws, dev):
         def step():
             for li in range(LAYERS):
                 ops.gqa_decode(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND", out=out[li],
-                               workspace=ws, max_kv_len=L)
+                               workspace=ws, max_kv_len=L, stable_prefix=True)
 
         step()
         torch.cuda.synchronize(dev)
@@ -604,7 +615,7 @@ def paged_bench(dev, reps: int) -> dict:
     def step():
         for li in range(LAYERS):
             ops.gqa_decode_paged(q[li], arenas[li], bt, qpos, max_kv_len=n_a, q_lens=qlens,
-                                 out=out[li], workspace=ws)
+                                 out=out[li], workspace=ws, stable_prefix=True)
 
     ms = _time_graph(step, dev, reps)
     per_layer = (n_a + n_b) * NKV * HD * 2 * 2
@@ -637,7 +648,7 @@ def long_ctx_bench(dev, reps: int, ctx: int = 131072) -> dict:
     def step():
         for li in range(layers):
             ops.gqa_decode(q[li], kv[li, 0], kv[li, 1], qpos, kv_layout="HND", out=out[li],
-                           workspace=ws)
+                           workspace=ws, stable_prefix=True)
 
     ms = _time_graph(step, dev, reps)
     byt = 2 * ctx * NKV * HD * 2

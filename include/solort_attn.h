@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define SOLORT_ATTN_ABI_VERSION 1
+#define SOLORT_ATTN_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define SOLORT_API __attribute__((visibility("default")))
@@ -81,7 +81,15 @@ extern "C" {
  * get out_f32 = 0, lse = -inf. These partials combine with solort_attn_lse_merge.
  *
  * Workspace: split-KV partials; query solort_attn_decode_workspace_size() with the same args.
+ *
+ * flags: SOLORT_DECODE_STABLE_PREFIX promises that q_pos, q_lens, the block table and every K/V
+ * row at a position below q_pos[b] were written before the kernel launched just before this call
+ * on the stream (earlier steps, host copies before a graph replay), so the call may read them
+ * while that kernel is still running: the key stream then starts during its tail. Rows at q_pos[b]
+ * and later (the tokens the previous kernel may just have appended), the queries and the
+ * workspace are touched only after it has finished, with or without the flag.
  */
+#define SOLORT_DECODE_STABLE_PREFIX 1u
 typedef struct SolortDecodeArgs {
   const void* q;
   int64_t q_stride_batch, q_stride_token, q_stride_head;
@@ -111,6 +119,7 @@ typedef struct SolortDecodeArgs {
 
   void* workspace;
   size_t workspace_bytes;
+  uint32_t flags; /* SOLORT_DECODE_* bits, 0 by default */
 } SolortDecodeArgs;
 
 SOLORT_API int solort_attn_decode_workspace_size(const SolortDecodeArgs* args, size_t* bytes);

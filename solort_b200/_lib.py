@@ -50,6 +50,7 @@ EXPORTED_SYMBOLS = (
 )
 
 MAX_RANKS = 8  # SOLORT_MAX_RANKS
+DECODE_STABLE_PREFIX = 1  # SOLORT_DECODE_STABLE_PREFIX
 IPC_HANDLE_BYTES = 64
 
 c_i32, c_i64, c_f32, c_vp, c_sz = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
@@ -83,6 +84,7 @@ class SolortDecodeArgs(ctypes.Structure):
         ("num_splits", c_i32),
         ("workspace", c_vp),
         ("workspace_bytes", c_sz),
+        ("flags", ctypes.c_uint32),
     ]
 
 

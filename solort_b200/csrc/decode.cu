@@ -83,6 +83,7 @@ struct Params {
   int q_vec16;  // q base and strides allow 16-byte loads
   int force_partial;  // one split still goes through the partials and the merge kernel
   int stages;  // ring depth: kMaxStages, or one less when a long block-table slice needs room
+  int stable_prefix;  // q_pos, q_lens, block table and keys below q_pos precede the previous kernel
   float scale_log2;
 };
 
@@ -159,7 +160,11 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
     flags[0] = 0;
     fence_mbarrier_init();
   }
-  pdl_wait();  // inputs and the workspace may belong to the kernel before this one
+  // Inputs and the workspace may belong to the kernel before this one. With stable_prefix the
+  // positions, the block table and the keys below q_pos were written before it, so they are read
+  // (and those keys requested) before waiting; everything else waits as usual.
+  const bool early = p.stable_prefix != 0;
+  if (!early) pdl_wait();
 
   const long long qpos = p.q_pos[b];
   const int qlen_b = p.q_lens ? min(p.q_lens[b], p.q_len) : p.q_len;
@@ -179,6 +184,7 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
 
   if (ntiles == 0) {
     // Nothing visible in this split: an empty partial (O = 0, LSE = -inf), or zero final rows.
+    if (early) pdl_wait();
     for (int idx = tid; idx < rows_b * (kHD / 4); idx += kThreads) {
       const int r = idx / (kHD / 4), c = (idx % (kHD / 4)) * 4;
       const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -231,9 +237,21 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
   };
 
   // Every stage but the last is filled at once; the last one first carries this CTA's query rows.
+  // Tiles whose keys all lie below q_pos go out before the wait when the prefix is stable.
   if (initial_issuer) {
     const int n0 = ntiles < nst - 1 ? ntiles : nst - 1;
-    for (int i = 0; i < n0; ++i) issue(i, i);
+    int i = 0;
+    if (early) {
+      const long long stable_end = qpos - p.kv_pos_offset;  // local keys below it are stable
+      while (i < n0 && min(t_begin + (i + 1) * kTile, t_end) <= stable_end) {
+        issue(i, i);
+        ++i;
+      }
+    }
+    if (early) pdl_wait();
+    for (; i < n0; ++i) issue(i, i);
+  } else if (early) {
+    pdl_wait();
   }
 
   // Query fragments (A operand, m16k16 per (mt, ks)). The 37-odd CTAs of a KV head all need the
@@ -927,6 +945,7 @@ int decode_impl(const SolortDecodeArgs* a, const SolortExchangeArgs* x, void* st
   prm.chunk = pl.chunk;
   prm.num_splits = pl.splits;
   prm.stages = pl.stages;
+  prm.stable_prefix = (a->flags & SOLORT_DECODE_STABLE_PREFIX) ? 1 : 0;
   prm.force_partial = pl.force_partial ? 1 : 0;
   prm.q_vec16 = aligned(a->q, 16) && ((a->q_stride_batch | a->q_stride_token | a->q_stride_head) & 7) == 0;
   prm.scale_log2 = a->scale * 1.4426950408889634f;

@@ -57,6 +57,7 @@ def _decode_args(
     q_lens: torch.Tensor | None,
     kv_pos_offset: int,
     num_splits: int,
+    stable_prefix: bool = False,
 ) -> _lib.SolortDecodeArgs:
     _check_cuda("q", q, torch.bfloat16)
     if q.dim() != 4 or q.shape[-1] != HEAD_DIM or q.stride(-1) != 1:
@@ -85,6 +86,7 @@ def _decode_args(
     a.max_kv_len = int(max_kv_len)
     a.scale = float(D ** -0.5 if scale is None else scale)
     a.num_splits = int(num_splits)
+    a.flags = _lib.DECODE_STABLE_PREFIX if stable_prefix else 0
     return a
 
 
@@ -154,6 +156,7 @@ def gqa_decode(
     workspace: torch.Tensor | None = None,
     q_lens: torch.Tensor | None = None,
     num_splits: int = 0,
+    stable_prefix: bool = False,
 ) -> torch.Tensor:
     """GQA attention of ``q [B, q_len, nh, 128]`` against one layer's static KV buffer.
 
@@ -162,7 +165,9 @@ def gqa_decode(
     (``"HND"``). ``q_pos`` (int64, ``[B]``, on the device) is the position of query row 0: row
     ``i`` sees keys ``0 .. q_pos + i`` -- decode (``:168,180-184``) with ``q_len == 1`` and verify
     (``:250,261-263``) with ``q_len == K + 1``. ``max_kv_len`` bounds the keys read (the decode
-    bucket ``bound``); it defaults to the buffer length.
+    bucket ``bound``); it defaults to the buffer length. ``stable_prefix``: ``q_pos`` and the keys
+    below it were written before the kernel launched just before this call (earlier steps), so
+    their loads may start during that kernel's tail (``SOLORT_DECODE_STABLE_PREFIX``).
     """
     cap, nkv, st, sh = _static_kv(k_cache, v_cache, kv_layout)
     if q_pos.numel() != q.shape[0]:
@@ -173,7 +178,7 @@ def gqa_decode(
         q, k_cache, v_cache, q_pos, stride_token=st, stride_head=sh, stride_page=0,
         kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
         scale=scale, max_kv_len=max_kv_len or cap, out=out, out_f32=None, lse_out=None,
-        q_lens=q_lens, kv_pos_offset=0, num_splits=num_splits)
+        q_lens=q_lens, kv_pos_offset=0, num_splits=num_splits, stable_prefix=stable_prefix)
     _run_decode(a, q.device, workspace)
     return out
 
@@ -184,14 +189,14 @@ class DecodeCall:
     buffers, which never move between decode steps; ``cuda_graph_executor.py:67-71``)."""
 
     def __init__(self, q, k_cache, v_cache, q_pos, *, kv_layout="NHD", scale=None,
-                 max_kv_len=None, out, workspace=None, num_splits=0):
+                 max_kv_len=None, out, workspace=None, num_splits=0, stable_prefix=False):
         cap, nkv, st, sh = _static_kv(k_cache, v_cache, kv_layout)
         self._keep = (q, k_cache, v_cache, q_pos, out)
         self.args = _decode_args(
             q, k_cache, v_cache, q_pos, stride_token=st, stride_head=sh, stride_page=0,
             kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
             scale=scale, max_kv_len=max_kv_len or cap, out=out, out_f32=None, lse_out=None,
-            q_lens=None, kv_pos_offset=0, num_splits=num_splits)
+            q_lens=None, kv_pos_offset=0, num_splits=num_splits, stable_prefix=stable_prefix)
         lib = _lib.load()
         need = ctypes.c_size_t(0)
         _lib.check(lib.solort_attn_decode_workspace_size(ctypes.byref(self.args), ctypes.byref(need)),
@@ -219,7 +224,7 @@ class ShardedDecodeCall:
 
     def __init__(self, q, k_shard, v_shard, q_pos, exchange, recv_slots: int, slot_stride: int,
                  num_ranks: int, *, kv_pos_offset=0, kv_layout="NHD", scale=None, out,
-                 workspace):
+                 workspace, stable_prefix=False):
         cap, nkv, st, sh = _static_kv(k_shard, v_shard, kv_layout)
         _check_cuda("out", out, torch.bfloat16)
         self._keep = (q, k_shard, v_shard, q_pos, out, workspace, exchange)
@@ -227,7 +232,7 @@ class ShardedDecodeCall:
             q, k_shard, v_shard, q_pos, stride_token=st, stride_head=sh, stride_page=0,
             kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
             scale=scale, max_kv_len=cap, out=None, out_f32=None, lse_out=None, q_lens=None,
-            kv_pos_offset=kv_pos_offset, num_splits=0)
+            kv_pos_offset=kv_pos_offset, num_splits=0, stable_prefix=stable_prefix)
         lib = _lib.load()
         need = ctypes.c_size_t(0)
         _lib.check(lib.solort_attn_decode_exchange_workspace_size(ctypes.byref(self.args),
@@ -303,6 +308,7 @@ def gqa_decode_paged(
     workspace: torch.Tensor | None = None,
     q_lens: torch.Tensor | None = None,
     num_splits: int = 0,
+    stable_prefix: bool = False,
 ) -> torch.Tensor:
     """GQA attention against one layer of SoloRT's paged arena.
 
@@ -311,7 +317,8 @@ def gqa_decode_paged(
     page allocator and prefix cache hand them out (shared prefix pages may appear in several
     rows). Logical position ``p`` lives at page ``block_table[b, p // P]``, row ``p % P``
     (``kv_cache.py:136-149``). ``q_pos``/``q_lens`` as in ``gqa_decode``; ``max_kv_len`` bounds
-    the keys any sequence may see.
+    the keys any sequence may see; ``stable_prefix`` as in ``gqa_decode`` (it also covers the
+    block table).
     """
     _check_cuda("kv_pages", kv_pages, torch.bfloat16)
     _check_cuda("block_table", block_table, torch.int32)
@@ -333,7 +340,7 @@ def gqa_decode_paged(
         stride_page=kv_pages.stride(0), kv_capacity=0, num_kv_heads=nkv,
         block_table=block_table, page_size=P, num_pages=num_pages, scale=scale,
         max_kv_len=max_kv_len, out=out, out_f32=None, lse_out=None, q_lens=q_lens,
-        kv_pos_offset=0, num_splits=num_splits)
+        kv_pos_offset=0, num_splits=num_splits, stable_prefix=stable_prefix)
     _run_decode(a, q.device, workspace)
     return out
 
@@ -409,6 +416,7 @@ def gqa_decode_exchange(
     max_kv_len: int | None = None,
     workspace: torch.Tensor | None = None,
     num_splits: int = 0,
+    stable_prefix: bool = False,
 ) -> None:
     """Decode over this rank's key shard and store the rank's partial ``(O, LSE)`` into its slot
     on every rank named by ``exchange`` (peer-memory stores of self-marking 64-bit words)."""
@@ -417,7 +425,8 @@ def gqa_decode_exchange(
         q, k_cache, v_cache, q_pos, stride_token=st, stride_head=sh, stride_page=0,
         kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
         scale=scale, max_kv_len=max_kv_len or cap, out=None, out_f32=None, lse_out=None,
-        q_lens=None, kv_pos_offset=kv_pos_offset, num_splits=num_splits)
+        q_lens=None, kv_pos_offset=kv_pos_offset, num_splits=num_splits,
+        stable_prefix=stable_prefix)
     lib = _lib.load()
     need = ctypes.c_size_t(0)
     _lib.check(lib.solort_attn_decode_exchange_workspace_size(ctypes.byref(a), ctypes.byref(need)),

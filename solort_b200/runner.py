@@ -263,7 +263,7 @@ class GraphQwen3Runner:
         def attend(li, q):
             return ops.gqa_decode(q.reshape(1, 1, self.nh, self.hd), self.kc[li], self.vc[li],
                                   self.pos_buf, scale=self.scale, max_kv_len=bound,
-                                  workspace=self.attn_ws)
+                                  workspace=self.attn_ws, stable_prefix=True)
 
         return self._layer_stack(x, 1, self.pos_buf, self.pos_buf, cos, sin, attend,
                                  lm_head=True).float()
@@ -323,7 +323,8 @@ class GraphQwen3Runner:
 
         def attend(li, q):
             return ops.gqa_decode(q.reshape(1, k1, self.nh, self.hd), self.kc[li], self.vc[li],
-                                  self.vpos0, scale=self.scale, workspace=self.attn_ws)
+                                  self.vpos0, scale=self.scale, workspace=self.attn_ws,
+                                  stable_prefix=True)
 
         return self._layer_stack(x, k1, self.vpos0, pos, cos, sin, attend, lm_head=True).float()
 

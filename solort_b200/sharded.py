@@ -180,15 +180,16 @@ class ShardedDecode:
 
     def layer(self, li: int, q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
               q_pos: torch.Tensor, kv_pos_offset: int, out: torch.Tensor,
-              workspace: torch.Tensor | None = None) -> torch.Tensor:
+              workspace: torch.Tensor | None = None, stable_prefix: bool = False) -> torch.Tensor:
         """Attention of ``q [B, q_len, nh, 128]`` over the whole sharded sequence of layer ``li``;
-        ``k_shard``/``v_shard`` are this rank's keys, first one at ``kv_pos_offset``."""
+        ``k_shard``/``v_shard`` are this rank's keys, first one at ``kv_pos_offset``
+        (``stable_prefix`` as in ``ops.gqa_decode``, peer exchange only)."""
         if self.px is not None:
             from solort_b200 import ops
 
             ops.gqa_decode_exchange(q, k_shard, v_shard, q_pos, self.px.send_args[li],
                                     kv_pos_offset=kv_pos_offset, kv_layout=self.kv_layout,
-                                    workspace=workspace)
+                                    workspace=workspace, stable_prefix=stable_prefix)
             return ops.exchange_merge(*self.px.recv(li), self.world, out)
         buf, o, lse, o_parts, lse_parts = self._views(li)
         self.partial_fn(q, k_shard, v_shard, q_pos, kv_pos_offset=kv_pos_offset,
@@ -201,7 +202,7 @@ class ShardedDecode:
 
     def prepared_layer(self, li: int, q: torch.Tensor, k_shard: torch.Tensor,
                        v_shard: torch.Tensor, q_pos: torch.Tensor, kv_pos_offset: int,
-                       out: torch.Tensor, workspace: torch.Tensor):
+                       out: torch.Tensor, workspace: torch.Tensor, stable_prefix: bool = False):
         """``layer`` with its arguments packed once (peer exchange only): a callable that launches
         the layer's two kernels on the current stream."""
         from solort_b200 import ops
@@ -210,7 +211,8 @@ class ShardedDecode:
             raise RuntimeError("prepared layers need exchange='p2p'")
         return ops.ShardedDecodeCall(q, k_shard, v_shard, q_pos, self.px.send_args[li],
                                      *self.px.recv(li), self.world, kv_pos_offset=kv_pos_offset,
-                                     kv_layout=self.kv_layout, out=out, workspace=workspace)
+                                     kv_layout=self.kv_layout, out=out, workspace=workspace,
+                                     stable_prefix=stable_prefix)
 
     def close(self) -> None:
         if self.px is not None:
