@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: partials cross GPUs by NVLink peer stores (p2p) or an NCCL all-gather")
     ap.add_argument("--prefill-T", type=int, nargs="+", default=[512, 1024, 4096])
+    ap.add_argument("--step-timeline", action="store_true",
+                    help="print the kernel-by-kernel critical path of one Qwen3-4B-shaped decode "
+                         "step (CUPTI timeline; diagnostic, not a bench value)")
     ap.add_argument("--no-stable-prefix", action="store_true",
                     help="decode calls without SOLORT_DECODE_STABLE_PREFIX (keys requested only "
                          "after the previous kernel finished)")
@@ -658,11 +661,9 @@ def long_ctx_bench(dev, reps: int, ctx: int = 131072) -> dict:
             "frac_of_measured_hbm": round(byt / (us * 1e-6) / 1e9 / _peaks()[0], 4)}
 
 
-def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512) -> dict:
-    """End-to-end greedy decode tok/s of the engine's CUDA-graph runner on a random-weight
-    Qwen3-4B-shaped model (36 layers, hidden 2560, 32/8 heads, hd 128, intermediate 9728, vocab
-    151936), the reference microbenchmark's tight loop (decode_gpu_argmax back to back, one sync
-    at the end; scripts/microbench_decode.py:80-84)."""
+def _qwen3_4b_runner(dev, max_len: int):
+    """A random-weight Qwen3-4B-shaped model (36 layers, hidden 2560, 32/8 heads, hd 128,
+    intermediate 9728, vocab 151936) and the engine's CUDA-graph runner over it."""
     import torch
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
@@ -677,10 +678,19 @@ def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512) -> dict:
     torch.manual_seed(0)
     with torch.device(dev):
         model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+    return model, GraphQwen3Runner(model, max_len)
+
+
+def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512) -> dict:
+    """End-to-end greedy decode tok/s of the engine's CUDA-graph runner on a random-weight
+    Qwen3-4B-shaped model, the reference microbenchmark's tight loop (decode_gpu_argmax back to
+    back, one sync at the end; scripts/microbench_decode.py:80-84)."""
+    import torch
+
     max_len = prompt_len + new_tokens + 16
-    prompt = torch.randint(0, cfg.vocab_size, (prompt_len,), device=dev)
+    model, runner = _qwen3_4b_runner(dev, max_len)
+    prompt = torch.randint(0, 151936, (prompt_len,), device=dev)
     with torch.no_grad():
-        runner = GraphQwen3Runner(model, max_len)
         first = int(runner.prefill(prompt).argmax(-1).item())
         cur = first
         for pos in range(prompt_len, prompt_len + new_tokens + 4):  # capture every bucket
@@ -748,8 +758,57 @@ def _peaks(tensor: bool = False):
         return 6650.0, "fallback 6.65 TB/s"
 
 
+def step_timeline(dev, prompt_len: int = 512) -> dict:
+    """Where one decode step of the Qwen3-4B-shaped runner spends its time: a CUPTI kernel
+    timeline (torch.profiler) of three graph replays; since launches overlap under PDL, each
+    kernel is charged the growth of the latest end time it causes (its critical-path share).
+    Diagnostic only: times taken under the profiler are not bench values."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    model, runner = _qwen3_4b_runner(dev, prompt_len + 64)
+    kinds = ("gemv_kernel", "prologue_kernel", "decode_kernel", "merge_kernel")
+    with torch.no_grad():
+        tok = runner.prefill(torch.randint(0, 151936, (prompt_len,), device=dev)).argmax(-1)
+        for i in range(8):
+            tok = runner.decode_gpu_argmax(tok.view(1), prompt_len + i)
+        torch.cuda.synchronize(dev)
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for i in range(3):
+                tok = runner.decode_gpu_argmax(tok.view(1), prompt_len + 8 + i)
+            torch.cuda.synchronize(dev)
+    evs = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                 if e.device_type == torch.autograd.DeviceType.CUDA)
+    step = evs[len(evs) // 3: 2 * len(evs) // 3]  # the middle replay
+    proj = ["qkv", "o", "gate_up", "down"]
+    shares, gi, last_end = {}, 0, step[0][0]
+    for start, end, name in step:
+        kind = next((k for k in kinds if k in name), "other (embedding, argmax, copies)")
+        if kind == "gemv_kernel":
+            kind = "gemv " + (proj[gi % 4] if gi < 4 * 36 else "lm_head")
+            gi += 1
+        grow = max(0.0, end - last_end)
+        last_end = max(last_end, end)
+        n, t = shares.get(kind, (0, 0.0))
+        shares[kind] = (n + 1, t + grow)
+    total = sum(t for _, t in shares.values())
+    mb = {"gemv qkv": 31.46, "gemv o": 20.97, "gemv gate_up": 99.61, "gemv down": 49.81,
+          "gemv lm_head": 777.9}
+    rows = {k: {"launches": n, "critical_path_us": round(t, 1), "share": round(t / total, 4),
+                **({"TBs_on_critical_path": round(mb[k] * n / t, 2)} if k in mb else {})}
+            for k, (n, t) in sorted(shares.items(), key=lambda kv: -kv[1][1])}
+    del runner, model
+    torch.cuda.empty_cache()
+    return {"step_us": round(total, 1), "context": prompt_len + 9, "kernels": rows}
+
+
 def main():
     args = parse_args()
+    if args.step_timeline:
+        import torch
+
+        print(json.dumps(step_timeline(torch.device("cuda", 0)), indent=1))
+        return
     if args.impl == "reference":
         run_reference_arm(args)
     elif args.workload == "prefill":

@@ -10,8 +10,8 @@
 //           of squares is accumulated in exactly the order of the add_rmsnorm kernel, so the two
 //           paths give the same bits; CTA 0 also writes bf16(x + delta) to x_out.
 //
-// Layout: eight warps per CTA, one output row per warp at a time; the grid strides over groups of
-// eight rows (a few CTAs per SM, staging amortised over the CTA's groups). Each lane keeps eight
+// Layout: eight warps per CTA, one output row per warp (or per pair of warps, below) at a time; the
+// grid strides over groups of rows (four CTAs per SM, staging amortised over the CTA's groups). Each lane keeps eight
 // 16-byte weight loads in flight (64 registers, four CTAs per SM), and the next row's first batch
 // is issued before the current row is reduced. The first batch is issued before the kernel waits
 // for its predecessor on the stream (programmatic dependent launch); W must therefore not be
@@ -149,52 +149,62 @@ __device__ __forceinline__ void stage_activations(const Params& p, bf16* act, fl
   }
 }
 
-template <int T>
+// S warps share each output row (S = 1 or 2, a template parameter so the S = 1 kernel carries no
+// split bookkeeping; four warps per row measured slower over the whole decode step): warp w takes row w / S of its group, chunk range part w % S of it.
+template <int T, int S>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ float red[kWarps];
+  __shared__ float part_sum[S > 1 ? 2 : 1][kWarps][T];
   bf16* act = reinterpret_cast<bf16*>(smem);  // [T][K]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int chunks = p.k / 8;
-  const int groups = (p.n + kWarps - 1) / kWarps;
+  constexpr int kRows = kWarps / S;  // rows per group
+  const int groups = (p.n + kRows - 1) / kRows;
+  const int part = S > 1 ? warp % S : 0;
+  // This warp's chunk range: whole 32-chunk slots, the last part ragged.
+  const int spp = S > 1 ? ((chunks + 31) / 32 + S - 1) / S : 0;
+  const int c_begin = S > 1 ? part * spp * 32 : 0;
+  const int c_end = S > 1 ? min(chunks, c_begin + spp * 32) : chunks;
   constexpr int kStep = 32 * kUnroll;
 
   auto load_first = [&](int row, uint4 (&wv)[kUnroll]) {
     const bf16* wrow = p.w + static_cast<int64_t>(row) * p.w_st;
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const int c = lane + u * 32;
-      wv[u] = (row < p.n && c < chunks) ? *reinterpret_cast<const uint4*>(wrow + c * 8)
-                                        : make_uint4(0u, 0u, 0u, 0u);
+      const int c = c_begin + lane + u * 32;
+      wv[u] = (row < p.n && c < c_end) ? *reinterpret_cast<const uint4*>(wrow + c * 8)
+                                       : make_uint4(0u, 0u, 0u, 0u);
     }
   };
 
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   uint4 wv[kUnroll];
-  load_first(blockIdx.x * kWarps + warp, wv);
+  load_first(blockIdx.x * kRows + warp / S, wv);
   asm volatile("griddepcontrol.wait;" ::: "memory");
   stage_activations<T>(p, act, red);
 
+  int buf = 0;
   for (int g = blockIdx.x; g < groups; g += gridDim.x) {
-    const int row = g * kWarps + warp;
+    const int row = g * kRows + warp / S;
     const bf16* wrow = p.w + static_cast<int64_t>(row) * p.w_st;
     float acc[T];
 #pragma unroll
     for (int tt = 0; tt < T; ++tt) acc[tt] = 0.f;
     if (row < p.n) {
-      for (int c0 = 0; c0 < chunks; c0 += kStep) {
-        if (c0 > 0) {
+      for (int c0 = c_begin; c0 < c_end; c0 += kStep) {
+        if (c0 > c_begin) {
 #pragma unroll
           for (int u = 0; u < kUnroll; ++u) {
             const int c = c0 + lane + u * 32;
-            wv[u] = c < chunks ? *reinterpret_cast<const uint4*>(wrow + c * 8)
-                               : make_uint4(0u, 0u, 0u, 0u);
+            wv[u] = c < c_end ? *reinterpret_cast<const uint4*>(wrow + c * 8)
+                              : make_uint4(0u, 0u, 0u, 0u);
           }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int c = c0 + lane + u * 32;
-          if (c < chunks) {
+          if (c < c_end) {
 #pragma unroll
             for (int tt = 0; tt < T; ++tt)
               dot8(acc[tt], wv[u], *reinterpret_cast<const uint4*>(act + tt * p.k + c * 8));
@@ -203,26 +213,48 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params
       }
     }
     // The next group's first batch goes out before this row is reduced and stored.
-    load_first((g + gridDim.x) * kWarps + warp, wv);
-    if (row < p.n) {
+    load_first((g + gridDim.x) * kRows + warp / S, wv);
+    if (S == 1) {
+      if (row < p.n) {
+#pragma unroll
+        for (int tt = 0; tt < T; ++tt) {
+          float v = acc[tt];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == 0 && tt < p.t) p.y[tt * p.y_st + row] = __float2bfloat16_rn(v);
+        }
+      }
+    } else {
+      // The row's partials meet in shared memory (double-buffered by group, one barrier per
+      // group) and its first warp sums them in warp order.
+      float mine = 0.f;
 #pragma unroll
       for (int tt = 0; tt < T; ++tt) {
         float v = acc[tt];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0 && tt < p.t) p.y[tt * p.y_st + row] = __float2bfloat16_rn(v);
+        if (lane == tt) mine = v;
       }
+      if (lane < T) part_sum[buf][warp][lane] = mine;
+      asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+      if (part == 0 && row < p.n && lane < p.t) {
+        float v = 0.f;
+#pragma unroll
+        for (int j = 0; j < S; ++j) v += part_sum[buf][warp + j][lane];
+        p.y[lane * p.y_st + row] = __float2bfloat16_rn(v);
+      }
+      buf ^= 1;
     }
   }
 }
 
-template <int T>
+template <int T, int S>
 int launch(const Params& p, size_t smem, int grid, cudaStream_t stream) {
   static unsigned configured = 0;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
   if (dev >= 32 || !(configured & (1u << dev))) {
-    if (cudaFuncSetAttribute(gemv_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemv_kernel<T, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kMaxStageBytes) != cudaSuccess)
       return SOLORT_ERR_CUDA;
     if (dev < 32) configured |= 1u << dev;
@@ -237,8 +269,24 @@ int launch(const Params& p, size_t smem, int grid, cudaStream_t stream) {
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, gemv_kernel<T>, p) != cudaSuccess) return SOLORT_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, gemv_kernel<T, S>, p) != cudaSuccess) return SOLORT_ERR_CUDA;
   return launch_status();
+}
+
+// Two warps share a row when it spans more than one batch of loads and there are too few rows to
+// keep every warp of a resident wave busy twice over (qkv, o_proj, down of Qwen3-4B; a row of
+// 9728 is five serial batches for one warp while half the resident warps idle). Whole decode step
+// of the Qwen3-4B shape: 359 -> 371 tokens/s.
+inline int default_split(int n, int k, int sm_count) {
+  const int spr = (k / 8 + 31) / 32;
+  return (spr > kUnroll && n < 2 * kWarps * sm_count * kCtasPerSm) ? 2 : 1;
+}
+
+template <int T>
+int launch_split(const Params& p, size_t smem, int split, int grid_cap, cudaStream_t s) {
+  const int rows = kWarps / split;
+  const int grid = std::min((p.n + rows - 1) / rows, grid_cap);
+  return split == 2 ? launch<T, 2>(p, smem, grid, s) : launch<T, 1>(p, smem, grid, s);
 }
 
 inline bool overlaps(const void* a, int64_t a_bytes, const void* b, int64_t b_bytes) {
@@ -301,13 +349,13 @@ extern "C" int solort_attn_gemv(const SolortGemvArgs* a, void* stream_v) {
     p.x_out_st = a->x_out_stride;
     p.eps = a->eps;
   }
-  const int groups = (a->n + gemv::kWarps - 1) / gemv::kWarps;
-  const int grid = std::min(groups, di.sm_count * gemv::kCtasPerSm);
+  const int split = gemv::default_split(a->n, a->k, di.sm_count);
+  const int cap = di.sm_count * gemv::kCtasPerSm;
   cudaStream_t s = static_cast<cudaStream_t>(stream_v);
   switch (T) {
-    case 1: return gemv::launch<1>(p, smem, grid, s);
-    case 2: return gemv::launch<2>(p, smem, grid, s);
-    case 4: return gemv::launch<4>(p, smem, grid, s);
-    default: return gemv::launch<8>(p, smem, grid, s);
+    case 1: return gemv::launch_split<1>(p, smem, split, cap, s);
+    case 2: return gemv::launch_split<2>(p, smem, split, cap, s);
+    case 4: return gemv::launch_split<4>(p, smem, split, cap, s);
+    default: return gemv::launch_split<8>(p, smem, split, cap, s);
   }
 }
