@@ -387,14 +387,14 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
           }
         }
       }
-      if (kChains == 2) {
+#pragma unroll
+      for (int ch = 1; ch < kChains; ++ch)
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) sc[0][mt][nt][e] += sc[kChains - 1][mt][nt][e];
-      }
+            for (int e = 0; e < 4; ++e) sc[0][mt][nt][e] += sc[ch][mt][nt][e];
       // Mask, scale to the exp2 domain, online softmax.
       uint32_t pa[MT][4];
 #pragma unroll
@@ -457,12 +457,19 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
       }
     }
     // Both warps of the pair are done with stage s: refill it with the pair's tile ns_pair on.
-    if (pair == 0)
-      asm volatile("bar.sync 1, 64;" ::: "memory");
-    else
-      asm volatile("bar.sync 2, 64;" ::: "memory");
-    if (flags[0]) break;
-    if (wip == 0 && lane == 0 && it + 2 * ns_pair < ntiles) issue(it + 2 * ns_pair, s);
+    // Without a refill (a split that fits the ring) the pair need not meet; the condition is the
+    // same for both warps of the pair. An abort is seen by the pair at its next meeting or after
+    // the loop.
+    if (it + 2 * ns_pair < ntiles) {
+      if (pair == 0)
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+      else
+        asm volatile("bar.sync 2, 64;" ::: "memory");
+      if (flags[0]) break;
+      if (wip == 0 && lane == 0) issue(it + 2 * ns_pair, s);
+    } else if (flags[0]) {
+      break;
+    }
   }
   __syncthreads();
 
