@@ -164,6 +164,17 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
   // positions, the block table and the keys below q_pos were written before it, so they are read
   // (and those keys requested) before waiting; everything else waits as usual.
   const bool early = p.stable_prefix != 0;
+  // Warm L2 with this CTA's query rows before waiting: only a cache hint (the rows themselves are
+  // read after the wait, so a predecessor that writes them is still respected).
+  if (consumer) {
+    const int rows_alloc = p.q_len * p.group;
+    for (int idx = tid; idx < rows_alloc * 2; idx += kWarps * 32) {
+      const int r = idx >> 1;
+      const bf16* src = p.q + b * p.q_sb + (r / p.group) * p.q_st +
+                        (kvh * p.group + r % p.group) * p.q_sh + (idx & 1) * 64;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
+    }
+  }
   if (!early) pdl_wait();
 
   const long long qpos = p.q_pos[b];
