@@ -431,6 +431,7 @@ def run_gpu_arm(args) -> None:
         line["paged"] = paged_bench(dev, max(3, args.steps // 4))
         line["long_ctx"] = long_ctx_bench(dev, max(2, args.steps // 10))
         line["decode_tok_s"] = tok_s_bench(dev)
+        line["decode_tok_s_qwen3_0.6b"] = tok_s_bench(dev, shape="qwen3-0.6b")
     if world == 1 and not args.no_prefill:
         line["prefill"] = prefill_bench(dev, args.steps, args.warmup, tuple(args.prefill_T))
         if not args.no_cpu_baseline:
@@ -661,16 +662,22 @@ def long_ctx_bench(dev, reps: int, ctx: int = 131072) -> dict:
             "frac_of_measured_hbm": round(byt / (us * 1e-6) / 1e9 / _peaks()[0], 4)}
 
 
-def _qwen3_4b_runner(dev, max_len: int):
-    """A random-weight Qwen3-4B-shaped model (36 layers, hidden 2560, 32/8 heads, hd 128,
+# Random-weight Qwen3 shapes for the end-to-end decode rate: (layers, hidden, intermediate,
+# query heads, kv heads); head_dim 128, vocab 151936, tied embeddings.
+QWEN3_SHAPES = {"qwen3-4b": (36, 2560, 9728, 32, 8), "qwen3-0.6b": (28, 1024, 3072, 16, 8)}
+
+
+def _qwen3_4b_runner(dev, max_len: int, shape: str = "qwen3-4b"):
+    """A random-weight Qwen3-shaped model (default 4B: 36 layers, hidden 2560, 32/8 heads, hd 128,
     intermediate 9728, vocab 151936) and the engine's CUDA-graph runner over it."""
     import torch
     from transformers import Qwen3Config, Qwen3ForCausalLM
 
     from solort_b200.runner import GraphQwen3Runner
 
-    cfg = Qwen3Config(vocab_size=151936, hidden_size=2560, intermediate_size=9728,
-                      num_hidden_layers=36, num_attention_heads=32, num_key_value_heads=8,
+    layers, hidden, inter, nh, nkv = QWEN3_SHAPES[shape]
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=hidden, intermediate_size=inter,
+                      num_hidden_layers=layers, num_attention_heads=nh, num_key_value_heads=nkv,
                       head_dim=128, max_position_embeddings=40960, rms_norm_eps=1e-6,
                       tie_word_embeddings=True)
     cfg.rope_parameters = {"rope_type": "default", "rope_theta": 1e6}
@@ -681,14 +688,15 @@ def _qwen3_4b_runner(dev, max_len: int):
     return model, GraphQwen3Runner(model, max_len)
 
 
-def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512) -> dict:
+def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512,
+                shape: str = "qwen3-4b") -> dict:
     """End-to-end greedy decode tok/s of the engine's CUDA-graph runner on a random-weight
-    Qwen3-4B-shaped model, the reference microbenchmark's tight loop (decode_gpu_argmax back to
+    Qwen3-shaped model, the reference microbenchmark's tight loop (decode_gpu_argmax back to
     back, one sync at the end; scripts/microbench_decode.py:80-84)."""
     import torch
 
     max_len = prompt_len + new_tokens + 16
-    model, runner = _qwen3_4b_runner(dev, max_len)
+    model, runner = _qwen3_4b_runner(dev, max_len, shape)
     prompt = torch.randint(0, 151936, (prompt_len,), device=dev)
     with torch.no_grad():
         first = int(runner.prefill(prompt).argmax(-1).item())
@@ -703,9 +711,9 @@ def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512) -> dict:
         tok.item()
         dt = time.perf_counter() - t0
     res = {"tok_s": round(new_tokens / dt, 1), "ms_per_token": round(dt * 1e3 / new_tokens, 3),
-           "model": "random-weight Qwen3-4B shape, bf16", "prompt": prompt_len,
+           "model": f"random-weight {shape} shape, bf16", "prompt": prompt_len,
            "new_tokens": new_tokens,
-           "published_reference_rtx4080_tok_s": 67.0}
+           "published_reference_rtx4080_tok_s": {"qwen3-4b": 67.0, "qwen3-0.6b": 160.3}[shape]}
     del runner, model
     torch.cuda.empty_cache()
     return res
