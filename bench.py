@@ -402,7 +402,7 @@ def run_gpu_arm(args) -> None:
             "peak_source": peaks[1],
             "algorithmic_bytes_per_launch": bytes_per_layer,
             "us_per_launch": round(per_call_us, 3),
-            "traffic": 33627648 if (world == 1 and ctx == 8192) else None,
+            "traffic": 33634560 if (world == 1 and ctx == 8192) else None,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
                               "decode_kernel launch of this workload "
                               "(profiles/decode_splitkv_qwen3-4b_L8192_launches.md)",
