@@ -92,11 +92,11 @@ __device__ __forceinline__ void stage_activations(const Params& p, bf16* act, fl
       const int src = tt < p.t ? tt : 0;
       uint4 v;
       if (p.mode == 0) {
-        v = *reinterpret_cast<const uint4*>(p.a + src * p.a_st + c * 8);
+        v = __ldcg(reinterpret_cast<const uint4*>(p.a + src * p.a_st + c * 8));
       } else {
         float g[8], u[8], o[8];
-        unpack8(*reinterpret_cast<const uint4*>(p.a + src * p.a_st + c * 8), g);
-        unpack8(*reinterpret_cast<const uint4*>(p.a + src * p.a_st + p.k + c * 8), u);
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(p.a + src * p.a_st + c * 8)), g);
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(p.a + src * p.a_st + p.k + c * 8)), u);
 #pragma unroll
         for (int i = 0; i < 8; ++i) o[i] = bf(g[i] / (1.f + expf(-g[i]))) * u[i];
         v = pack8(o);
@@ -116,10 +116,10 @@ __device__ __forceinline__ void stage_activations(const Params& p, bf16* act, fl
     float ss = 0.f;
     for (int c = tid; c < chunks; c += kThreads) {
       float v[8];
-      unpack8(*reinterpret_cast<const uint4*>(p.a + src * p.a_st + c * 8), v);
+      unpack8(__ldcg(reinterpret_cast<const uint4*>(p.a + src * p.a_st + c * 8)), v);
       if (p.delta) {
         float d[8];
-        unpack8(*reinterpret_cast<const uint4*>(p.delta + src * p.delta_st + c * 8), d);
+        unpack8(__ldcg(reinterpret_cast<const uint4*>(p.delta + src * p.delta_st + c * 8)), d);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = bf(v[i] + d[i]);
       }
@@ -150,40 +150,44 @@ __device__ __forceinline__ void stage_activations(const Params& p, bf16* act, fl
 }
 
 // S warps share each output row (S = 1 or 2, a template parameter so the S = 1 kernel carries no
-// split bookkeeping; four warps per row measured slower over the whole decode step): warp w takes row w / S of its group, chunk range part w % S of it.
+// split bookkeeping; four warps per row measured slower over the whole decode step): warp w takes
+// row w / S of its group, chunk range part w % S of it.
+template <int S>
+struct RowSplit {
+  int part, c_begin, c_end;
+  __device__ __forceinline__ RowSplit(int warp, int chunks) {
+    part = S > 1 ? warp % S : 0;
+    const int spp = S > 1 ? ((chunks + 31) / 32 + S - 1) / S : 0;  // whole 32-chunk slots
+    c_begin = S > 1 ? part * spp * 32 : 0;
+    c_end = S > 1 ? min(chunks, c_begin + spp * 32) : chunks;
+  }
+};
+
+// The first batch of loads of this warp's part of `row` (zeros past the matrix).
+template <int S>
+__device__ __forceinline__ void load_first(const Params& p, const RowSplit<S>& rs, int row,
+                                           uint4 (&wv)[kUnroll]) {
+  const int lane = threadIdx.x & 31;
+  const bf16* wrow = p.w + static_cast<int64_t>(row) * p.w_st;
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int c = rs.c_begin + lane + u * 32;
+    wv[u] = (row < p.n && c < rs.c_end) ? *reinterpret_cast<const uint4*>(wrow + c * 8)
+                                        : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// Rows of groups blockIdx.x, + gridDim.x, ... against the staged activations; `wv` holds the first
+// group's first batch on entry.
 template <int T, int S>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ float red[kWarps];
+__device__ __forceinline__ void stream_rows(const Params& p, const bf16* act,
+                                            uint4 (&wv)[kUnroll]) {
   __shared__ float part_sum[S > 1 ? 2 : 1][kWarps][T];
-  bf16* act = reinterpret_cast<bf16*>(smem);  // [T][K]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int chunks = p.k / 8;
+  const RowSplit<S> rs(warp, p.k / 8);
   constexpr int kRows = kWarps / S;  // rows per group
   const int groups = (p.n + kRows - 1) / kRows;
-  const int part = S > 1 ? warp % S : 0;
-  // This warp's chunk range: whole 32-chunk slots, the last part ragged.
-  const int spp = S > 1 ? ((chunks + 31) / 32 + S - 1) / S : 0;
-  const int c_begin = S > 1 ? part * spp * 32 : 0;
-  const int c_end = S > 1 ? min(chunks, c_begin + spp * 32) : chunks;
   constexpr int kStep = 32 * kUnroll;
-
-  auto load_first = [&](int row, uint4 (&wv)[kUnroll]) {
-    const bf16* wrow = p.w + static_cast<int64_t>(row) * p.w_st;
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int c = c_begin + lane + u * 32;
-      wv[u] = (row < p.n && c < c_end) ? *reinterpret_cast<const uint4*>(wrow + c * 8)
-                                       : make_uint4(0u, 0u, 0u, 0u);
-    }
-  };
-
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  uint4 wv[kUnroll];
-  load_first(blockIdx.x * kRows + warp / S, wv);
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  stage_activations<T>(p, act, red);
-
   int buf = 0;
   for (int g = blockIdx.x; g < groups; g += gridDim.x) {
     const int row = g * kRows + warp / S;
@@ -192,19 +196,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params
 #pragma unroll
     for (int tt = 0; tt < T; ++tt) acc[tt] = 0.f;
     if (row < p.n) {
-      for (int c0 = c_begin; c0 < c_end; c0 += kStep) {
-        if (c0 > c_begin) {
+      for (int c0 = rs.c_begin; c0 < rs.c_end; c0 += kStep) {
+        if (c0 > rs.c_begin) {
 #pragma unroll
           for (int u = 0; u < kUnroll; ++u) {
             const int c = c0 + lane + u * 32;
-            wv[u] = c < c_end ? *reinterpret_cast<const uint4*>(wrow + c * 8)
-                              : make_uint4(0u, 0u, 0u, 0u);
+            wv[u] = c < rs.c_end ? *reinterpret_cast<const uint4*>(wrow + c * 8)
+                                 : make_uint4(0u, 0u, 0u, 0u);
           }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int c = c0 + lane + u * 32;
-          if (c < c_end) {
+          if (c < rs.c_end) {
 #pragma unroll
             for (int tt = 0; tt < T; ++tt)
               dot8(acc[tt], wv[u], *reinterpret_cast<const uint4*>(act + tt * p.k + c * 8));
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params
       }
     }
     // The next group's first batch goes out before this row is reduced and stored.
-    load_first((g + gridDim.x) * kRows + warp / S, wv);
+    load_first<S>(p, rs, (g + gridDim.x) * kRows + warp / S, wv);
     if (S == 1) {
       if (row < p.n) {
 #pragma unroll
@@ -237,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params
       }
       if (lane < T) part_sum[buf][warp][lane] = mine;
       asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
-      if (part == 0 && row < p.n && lane < p.t) {
+      if (rs.part == 0 && row < p.n && lane < p.t) {
         float v = 0.f;
 #pragma unroll
         for (int j = 0; j < S; ++j) v += part_sum[buf][warp + j][lane];
@@ -246,6 +250,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params
       buf ^= 1;
     }
   }
+}
+
+template <int T, int S>
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ float red[kWarps];
+  bf16* act = reinterpret_cast<bf16*>(smem);  // [T][K]
+  const int warp = threadIdx.x >> 5;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  uint4 wv[kUnroll];
+  load_first<S>(p, RowSplit<S>(warp, p.k / 8), blockIdx.x * (kWarps / S) + warp / S, wv);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  stage_activations<T>(p, act, red);
+  stream_rows<T, S>(p, act, wv);
 }
 
 template <int T, int S>
@@ -295,6 +313,7 @@ inline bool overlaps(const void* a, int64_t a_bytes, const void* b, int64_t b_by
 }
 
 }  // namespace gemv
+
 }  // namespace solort
 
 using namespace solort;

@@ -93,3 +93,4 @@ def test_gemv_fused_norm_rejects_aliased_residual():
     w = torch.randn(64, 256, device="cuda").to(torch.bfloat16)
     with pytest.raises(RuntimeError):
         ops.gemv(x, w, norm_weight=nw, delta=d, x_out=x)
+
