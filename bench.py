@@ -432,6 +432,7 @@ def run_gpu_arm(args) -> None:
         line["long_ctx"] = long_ctx_bench(dev, max(2, args.steps // 10))
         line["decode_tok_s"] = tok_s_bench(dev)
         line["decode_tok_s_qwen3_0.6b"] = tok_s_bench(dev, shape="qwen3-0.6b")
+        line["decode_tok_s_single_graph"] = tok_s_bench(dev, single_graph=True)
     if world == 1 and not args.no_prefill:
         line["prefill"] = prefill_bench(dev, args.steps, args.warmup, tuple(args.prefill_T))
         if not args.no_cpu_baseline:
@@ -667,7 +668,7 @@ def long_ctx_bench(dev, reps: int, ctx: int = 131072) -> dict:
 QWEN3_SHAPES = {"qwen3-4b": (36, 2560, 9728, 32, 8), "qwen3-0.6b": (28, 1024, 3072, 16, 8)}
 
 
-def _qwen3_4b_runner(dev, max_len: int, shape: str = "qwen3-4b"):
+def _qwen3_4b_runner(dev, max_len: int, shape: str = "qwen3-4b", single_graph: bool = False):
     """A random-weight Qwen3-shaped model (default 4B: 36 layers, hidden 2560, 32/8 heads, hd 128,
     intermediate 9728, vocab 151936) and the engine's CUDA-graph runner over it."""
     import torch
@@ -685,18 +686,18 @@ def _qwen3_4b_runner(dev, max_len: int, shape: str = "qwen3-4b"):
     torch.manual_seed(0)
     with torch.device(dev):
         model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
-    return model, GraphQwen3Runner(model, max_len)
+    return model, GraphQwen3Runner(model, max_len, single_decode_graph=single_graph)
 
 
 def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512,
-                shape: str = "qwen3-4b") -> dict:
+                shape: str = "qwen3-4b", single_graph: bool = False) -> dict:
     """End-to-end greedy decode tok/s of the engine's CUDA-graph runner on a random-weight
     Qwen3-shaped model, the reference microbenchmark's tight loop (decode_gpu_argmax back to
     back, one sync at the end; scripts/microbench_decode.py:80-84)."""
     import torch
 
     max_len = prompt_len + new_tokens + 16
-    model, runner = _qwen3_4b_runner(dev, max_len, shape)
+    model, runner = _qwen3_4b_runner(dev, max_len, shape, single_graph)
     prompt = torch.randint(0, 151936, (prompt_len,), device=dev)
     with torch.no_grad():
         first = int(runner.prefill(prompt).argmax(-1).item())
@@ -712,6 +713,7 @@ def tok_s_bench(dev, new_tokens: int = 256, prompt_len: int = 512,
         dt = time.perf_counter() - t0
     res = {"tok_s": round(new_tokens / dt, 1), "ms_per_token": round(dt * 1e3 / new_tokens, 3),
            "model": f"random-weight {shape} shape, bf16", "prompt": prompt_len,
+           "decode_graphs": "one for every length" if single_graph else "one per length bucket",
            "new_tokens": new_tokens,
            "published_reference_rtx4080_tok_s": {"qwen3-4b": 67.0, "qwen3-0.6b": 160.3}[shape]}
     del runner, model

@@ -46,7 +46,7 @@ class GraphQwen3Runner:
     GEMV_MAX_ROWS = 1  # weight-streaming projections for one token row; cuBLAS from two rows on
 
     def __init__(self, model, max_len: int, prologue: str = "fused", glue: str = "fused",
-                 proj: str = "gemv") -> None:
+                 proj: str = "gemv", single_decode_graph: bool = False) -> None:
         if prologue not in ("fused", "torch") or glue not in ("fused", "torch") or \
                 proj not in ("gemv", "torch"):
             raise ValueError((prologue, glue, proj))
@@ -90,8 +90,11 @@ class GraphQwen3Runner:
         self.vc = torch.zeros(shape, device=self.dev, dtype=self.dt)
         self.tok_buf = torch.zeros(1, dtype=torch.long, device=self.dev)
         self.pos_buf = torch.zeros(1, dtype=torch.long, device=self.dev)
-        self.buckets = sorted({b for b in (128, 256, 512, 1024, 2048, 4096) if b < self.max_len}
-                              | {self.max_len})
+        # The engine reads the live length from pos_buf, so one graph sized for max_len serves
+        # every position (single_decode_graph); the buckets remain the default because a bound far
+        # above the live length makes most splits of the decode grid empty.
+        self.buckets = [self.max_len] if single_decode_graph else sorted(
+            {b for b in (128, 256, 512, 1024, 2048, 4096) if b < self.max_len} | {self.max_len})
         self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self._logits: dict[int, torch.Tensor] = {}
         self._tok: dict[int, torch.Tensor] = {}

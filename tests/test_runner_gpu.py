@@ -105,3 +105,26 @@ def test_verify_and_chunked_decode_match_reference_runner():
         vr = ref.verify(drafts, pos + 4).argmax(-1).tolist()
         vo = ours.verify(drafts, pos + 4).argmax(-1).tolist()
         assert vo == vr
+
+
+def test_single_decode_graph_gives_the_bucketed_stream():
+    """One decode graph for every position (the engine reads the live length from pos_buf) gives
+    the logits of one graph per bucket: teacher-forced along the bucketed stream across the 128
+    bucket, within 2e-2, argmax equal except at near-ties (the split plans differ, so the fp32
+    merge order does)."""
+    from solort_b200.runner import GraphQwen3Runner
+
+    model = _model(2, 32, 8, 1024, 2048, 4096, seed=4)
+    prompt = torch.randint(0, 4096, (100,), generator=torch.Generator().manual_seed(2)).cuda()
+    with torch.no_grad():
+        bucketed = GraphQwen3Runner(model, 512)
+        single = GraphQwen3Runner(model, 512, single_decode_graph=True)
+        assert single.buckets == [512]
+        stream = bucketed.greedy(prompt, 40)
+        la = _teacher_forced(GraphQwen3Runner(model, 512), prompt, stream)
+        lb = _teacher_forced(single, prompt, stream)
+    for step, (a, b) in enumerate(zip(la, lb)):
+        assert (a - b).abs().max().item() <= 2e-2, step
+        if a.argmax().item() != b.argmax().item():
+            top2 = a.flatten().topk(2).values
+            assert (top2[0] - top2[1]).item() <= 4e-2, step
