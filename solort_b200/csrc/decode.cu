@@ -56,6 +56,7 @@ struct Shape {
   static constexpr int kThreads = kProducerWarp ? 160 : 128;
 };
 constexpr int kMaxPagedChunk = 16384;       // tokens per split at most with a block table
+constexpr int kMinSplitTiles = 4;           // default plans: at least 128 keys per split
 constexpr int kMergeWarps = 8;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -748,8 +749,11 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl, bool force_partial = false) {
   // Two CTAs per SM are resident; size the splits so the grid is one such wave.
   const int64_t resident = 2ll * di.sm_count;
   const int64_t heads = static_cast<int64_t>(a->batch) * a->num_kv_heads;
-  const int64_t target =
-      a->num_splits > 0 ? a->num_splits : (resident / heads > 1 ? resident / heads : 1);
+  // One resident wave of splits, but at least kMinSplitTiles tiles per split: a split of one or
+  // two tiles is all fixed cost (set-up, combine, partial store) and adds a partial to the merge.
+  const int64_t wave = resident / heads > 1 ? resident / heads : 1;
+  const int64_t by_len = ceil_div(pl->kv_limit, static_cast<int64_t>(kMinSplitTiles) * kTile);
+  const int64_t target = a->num_splits > 0 ? a->num_splits : (by_len < wave ? by_len : wave);
   int64_t chunk = ceil_div(ceil_div(pl->kv_limit, target), kBox) * kBox;
   if (pl->paged && chunk > kMaxPagedChunk) chunk = kMaxPagedChunk;
   pl->chunk = static_cast<int>(chunk);
