@@ -10,16 +10,19 @@
 //           of squares is accumulated in exactly the order of the add_rmsnorm kernel, so the two
 //           paths give the same bits; CTA 0 also writes bf16(x + delta) to x_out.
 //
-// Layout: eight warps per CTA, one output row per warp (or per pair of warps, below) at a time; the
-// grid strides over groups of rows (four CTAs per SM, staging amortised over the CTA's groups). Each lane keeps eight
-// 16-byte weight loads in flight (64 registers, four CTAs per SM), and the next row's first batch
-// is issued before the current row is reduced. The first batch is issued before the kernel waits
-// for its predecessor on the stream (programmatic dependent launch); W must therefore not be
-// written by the kernel just before this one (model weights are not).
+// Layout: eight warps per CTA, one output row per warp (or per pair of warps, below) at a time; a
+// grid of four CTAs per SM (64 registers; fewer fit when t * K * 2 bytes of staged activations
+// are large, and the grid then runs in waves) strides over groups of rows, so the staging is
+// amortised over a CTA's groups. Each lane keeps eight 16-byte weight loads in flight, and the next
+// group's first batch is issued before the current row is reduced. The first batch is issued
+// before the kernel waits for its predecessor on the stream (programmatic dependent launch); W
+// must therefore not be written by the kernel just before this one (model weights are not).
 //
-// Measured alternative not kept: a persistent CTA per SM streaming its rows with bulk async copies
-// into a ~200 KB shared-memory ring (deep prefetch independent of registers) was ~10-15% slower
-// over a whole decode step: the large-smem CTA cannot overlap the kernels before and after it.
+// Measured alternatives not kept (whole decode step): a persistent CTA per SM streaming its rows
+// with bulk async copies into a ~200 KB shared-memory ring (10-15% slower: the large-smem CTA
+// cannot overlap the kernels before and after it), a double-buffered register pipeline (half the
+// resident warps), ten loads per lane in flight, and the whole MLP as one launch with a grid
+// barrier between gate_up and down (the barrier cost more than the kernel boundary).
 #include <math.h>
 
 #include <algorithm>
