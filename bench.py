@@ -43,8 +43,9 @@ def parse_args():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="also time L in {128..8192}")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode",
-                    help="decode: BASELINE config 2 (+ prefill section); prefill: config 3 only")
+    ap.add_argument("--workload", choices=["decode", "prefill", "paged"], default="decode",
+                    help="decode: BASELINE config 2 (+ prefill section); prefill: config 3 only; "
+                         "paged: config 4 only (the default line's paged section alone)")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: partials cross GPUs by NVLink peer stores (p2p) or an NCCL all-gather")
@@ -752,6 +753,25 @@ def cpu_prefill_ms(T: int, threads: int) -> float:
     return (time.perf_counter() - t0) / n * 1e3
 
 
+def run_paged_workload(args) -> None:
+    """BASELINE config 4 alone, one GPU (the paged path runs as replicas only)."""
+    import torch
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    res = paged_bench(dev, max(3, args.steps))
+    peak = _peaks()
+    line = {"metric": "paged decode+verify HBM GB/s", "value": res["GBs"], "unit": "GB/s",
+            "n_gpus": 1, "steps": max(3, args.steps), "warmup": 3,
+            "ms_per_step": round(res["us_per_layer"] * LAYERS / 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "qwen3-4b paged decode + K=4 verify (BASELINE config 4)",
+                       "page_size": 16, "ctx": 16384, "layers": LAYERS},
+            "frac_of_measured_hbm": round(res["GBs"] / peak[0], 4), "peak_source": peak[1],
+            "paged": res}
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill_workload(args) -> None:
     import torch
 
@@ -838,6 +858,8 @@ def main():
         run_reference_arm(args)
     elif args.workload == "prefill":
         run_prefill_workload(args)
+    elif args.workload == "paged":
+        run_paged_workload(args)
     else:
         run_gpu_arm(args)
 
