@@ -25,6 +25,7 @@
 // i at vpos0+i sees keys <= vpos0+i) and the paged addressing of src/solort/cache/kv_cache.py:
 // 136-149 (slot = block_table[pos // P] * P + pos % P).
 #include <math.h>
+#include <string.h>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -823,6 +824,51 @@ int launch_merge(const MergeParams& mp, cudaStream_t stream) {
   return launch_status();
 }
 
+// The K and V tensor maps of recent calls. An encoding depends only on the base pointers, extents,
+// strides and box, which a decode step repeats layer after layer, while encoding costs host time
+// on every call; a hit returns the same bytes the encoder would. Direct-mapped, one entry per
+// slot, guarded by a mutex (callers may share the library across threads).
+struct KvMapEntry {
+  bool valid;
+  const void* k;
+  const void* v;
+  uint64_t dims[4];
+  uint64_t strides[3];
+  uint32_t box[4];
+  CUtensorMap tk, tv;
+};
+
+int cached_kv_maps(const void* k, const void* v, const uint64_t* dims, const uint64_t* strides,
+                   const uint32_t* box, CUtensorMap* tk, CUtensorMap* tv) {
+  constexpr int kSlots = 128;
+  static std::mutex mu;
+  static KvMapEntry cache[kSlots];
+  uint64_t h = reinterpret_cast<uintptr_t>(k) ^ (reinterpret_cast<uintptr_t>(v) << 7);
+  for (int i = 0; i < 4; ++i) h = h * 1000003u ^ dims[i] ^ (static_cast<uint64_t>(box[i]) << 40);
+  for (int i = 0; i < 3; ++i) h = h * 1000003u ^ strides[i];
+  KvMapEntry& e = cache[(h ^ (h >> 29)) % kSlots];
+  std::lock_guard<std::mutex> lock(mu);
+  if (e.valid && e.k == k && e.v == v && !memcmp(e.dims, dims, sizeof(e.dims)) &&
+      !memcmp(e.strides, strides, sizeof(e.strides)) && !memcmp(e.box, box, sizeof(e.box))) {
+    *tk = e.tk;
+    *tv = e.tv;
+    return SOLORT_OK;
+  }
+  int rc = encode_bf16_map(tk, k, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != SOLORT_OK) return rc;
+  rc = encode_bf16_map(tv, v, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != SOLORT_OK) return rc;
+  e.valid = true;
+  e.k = k;
+  e.v = v;
+  memcpy(e.dims, dims, sizeof(e.dims));
+  memcpy(e.strides, strides, sizeof(e.strides));
+  memcpy(e.box, box, sizeof(e.box));
+  e.tk = *tk;
+  e.tv = *tv;
+  return SOLORT_OK;
+}
+
 int build_kv_maps(const SolortDecodeArgs* a, const Plan& pl, CUtensorMap* tk, CUtensorMap* tv,
                   int* tok_coord, int* box_rows) {
   const int64_t st = a->kv_stride_token, sh = a->kv_stride_head;
@@ -868,9 +914,7 @@ int build_kv_maps(const SolortDecodeArgs* a, const Plan& pl, CUtensorMap* tk, CU
     strides[2] = align_up(strides[1] * dims[2], 16);
   }
   box[3] = 1;
-  int rc = encode_bf16_map(tk, a->k, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc != SOLORT_OK) return rc;
-  return encode_bf16_map(tv, a->v, 4, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+  return cached_kv_maps(a->k, a->v, dims, strides, box, tk, tv);
 }
 
 void fill_output_fields(const SolortDecodeArgs* a, Params* prm) {
