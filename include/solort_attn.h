@@ -10,6 +10,12 @@
  * negative SOLORT_ERR_* code; no exception crosses the ABI and nothing falls back to another
  * implementation.
  *
+ * State the library keeps: on the host, per-device properties, one-time kernel attribute set-up
+ * and a small cache of encoded K/V tensor maps keyed by every input of the encoding (a hit is the
+ * descriptor a fresh encoding would give, so freed and reused buffers are harmless); on each
+ * device, the status flags read by solort_attn_device_status and the static scratch array of
+ * solort_attn_decode_static_scratch. Calls from several host threads are safe.
+ *
  * The reference (owen920831/SoloRT) computes this attention inline in torch; the entry points
  * replace these call sites (paths inside the reference project):
  *   solort_attn_decode, q_len == 1, static KV:
