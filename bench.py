@@ -43,9 +43,12 @@ def parse_args():
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="also time L in {128..8192}")
-    ap.add_argument("--workload", choices=["decode", "prefill", "paged"], default="decode",
+    ap.add_argument("--workload", choices=["decode", "prefill", "paged", "long"], default="decode",
                     help="decode: BASELINE config 2 (+ prefill section); prefill: config 3 only; "
-                         "paged: config 4 only (the default line's paged section alone)")
+                         "paged: config 4 only; long: the 131072-key decode (config 5 on one "
+                         "GPU) only (the default line's paged / long_ctx sections alone)")
+    ap.add_argument("--layers", type=int, default=36,
+                    help="--workload long: layers of 512 MiB of K+V each (36 as in the model)")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: partials cross GPUs by NVLink peer stores (p2p) or an NCCL all-gather")
@@ -649,14 +652,13 @@ def paged_bench(dev, reps: int) -> dict:
                         "36 layers x 112 MB arenas"}
 
 
-def long_ctx_bench(dev, reps: int, ctx: int = 131072) -> dict:
+def long_ctx_bench(dev, reps: int, ctx: int = 131072, layers: int = 36) -> dict:
     """BASELINE config 5 on one GPU: 32/8 heads, one query at position ctx - 1 over 131072 keys per
     layer (512 MiB of K+V), 36 layers (18 GiB)."""
     import torch
 
     from solort_b200 import ops
 
-    layers = 36
     kv = torch.empty(layers, 2, NKV, ctx, HD, dtype=torch.bfloat16, device=dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(77)
@@ -675,7 +677,8 @@ def long_ctx_bench(dev, reps: int, ctx: int = 131072) -> dict:
     byt = 2 * ctx * NKV * HD * 2
     us = ms * 1e3 / layers
     del kv
-    return {"ctx": ctx, "us_per_layer": round(us, 2), "GBs": round(byt / (us * 1e-6) / 1e9, 1),
+    return {"ctx": ctx, "layers": layers, "us_per_layer": round(us, 2),
+            "GBs": round(byt / (us * 1e-6) / 1e9, 1),
             "frac_of_measured_hbm": round(byt / (us * 1e-6) / 1e9 / _peaks()[0], 4)}
 
 
@@ -772,6 +775,24 @@ def run_paged_workload(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_long_workload(args) -> None:
+    """The 131072-key decode (BASELINE config 5 on one GPU) alone."""
+    import torch
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    res = long_ctx_bench(dev, max(3, args.steps), layers=args.layers)
+    line = {"metric": "long-context decode-attn HBM GB/s", "value": res["GBs"], "unit": "GB/s",
+            "n_gpus": 1, "steps": max(3, args.steps), "warmup": 3,
+            "ms_per_step": round(res["us_per_layer"] * args.layers / 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "qwen3-4b decode over 131072 keys (BASELINE config 5, 1 GPU)",
+                       "layers": args.layers},
+            "peak_source": _peaks()[1], "long_ctx": res}
+    print(json.dumps(line), flush=True)
+
+
 def run_prefill_workload(args) -> None:
     import torch
 
@@ -860,6 +881,8 @@ def main():
         run_prefill_workload(args)
     elif args.workload == "paged":
         run_paged_workload(args)
+    elif args.workload == "long":
+        run_long_workload(args)
     else:
         run_gpu_arm(args)
 
