@@ -362,3 +362,63 @@ class GraphQwen3Runner:
             toks.append(self.decode_argmax(toks[-1], pos))
             pos += 1
         return toks
+
+
+def accept_drafts(proposals: list[int], target_next: list[int]) -> list[int]:
+    """Greedy speculative acceptance (the rule of ``SpecCudaGraphQwen3Executor._spec_round``,
+    ``src/solort/model/cuda_graph_executor.py:476-481``): ``target_next[i]`` is the target's argmax
+    after ``i`` drafts (``len(proposals) + 1`` entries). The drafts are taken while they equal the
+    target's choice; the target's token after the last accepted draft closes the round. Returns the
+    round's new tokens, ``accepted + 1`` of them."""
+    k = len(proposals)
+    if len(target_next) != k + 1:
+        raise ValueError(f"need {k + 1} target tokens for {k} drafts, got {len(target_next)}")
+    accepted = 0
+    while accepted < k and proposals[accepted] == target_next[accepted]:
+        accepted += 1
+    return list(proposals[:accepted]) + [target_next[accepted]]
+
+
+def spec_round(target: GraphQwen3Runner, draft: GraphQwen3Runner, last_token: int, pos: int,
+               k: int) -> list[int]:
+    """One speculative round (``cuda_graph_executor.py:463-482``): ``last_token`` sits at ``pos``;
+    the draft runner proposes ``k`` tokens by back-to-back GPU-resident decode replays, the target
+    scores ``[last_token, drafts]`` at ``pos .. pos + k`` in one verify replay (which also writes
+    their KV), and ``accept_drafts`` picks the new tokens. When every draft is accepted the draft
+    runner also decodes its last proposal at ``pos + k``, so its KV covers every position the next
+    round starts after. One host synchronisation per round."""
+    last = torch.tensor([int(last_token)], dtype=torch.long, device=target.dev)
+    proposals, cur = [], last
+    for i in range(k):
+        cur = draft.decode_gpu(cur, pos + i)
+        proposals.append(cur)
+    prop = torch.cat(proposals)
+    tgt = target.verify(torch.cat([last, prop]), pos).argmax(-1)
+    host = torch.cat([prop, tgt]).tolist()
+    new = accept_drafts(host[:k], host[k:])
+    if len(new) == k + 1:
+        draft.decode_gpu(prop[k - 1:k], pos + k)
+    return new
+
+
+def speculative_greedy(target: GraphQwen3Runner, draft: GraphQwen3Runner, prompt: torch.Tensor,
+                       steps: int, k: int = 4) -> tuple[list[int], list[int]]:
+    """Greedy generation with a draft model, as the reference's speculative executor runs it: both
+    runners prefill the prompt, the target's prefill argmax is the first token, then speculative
+    rounds until ``steps`` more tokens exist; near ``max_len`` (where a round would not fit) the
+    target decodes single tokens (``:450-452``). Returns the tokens (``steps + 1``, like
+    ``GraphQwen3Runner.greedy``) and each round's accepted draft count."""
+    toks = [int(target.prefill(prompt).argmax(-1).item())]
+    draft.prefill(prompt)
+    pos = int(prompt.shape[0])  # position of toks[-1]
+    accepted = []
+    while len(toks) < steps + 1:
+        if pos + k + 2 >= min(target.max_len, draft.max_len):
+            toks.append(target.decode_argmax(toks[-1], pos))
+            pos += 1
+            continue
+        new = spec_round(target, draft, toks[-1], pos, k)
+        accepted.append(len(new) - 1)
+        toks += new
+        pos += len(new)
+    return toks[:steps + 1], accepted

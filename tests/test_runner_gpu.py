@@ -128,3 +128,36 @@ def test_single_decode_graph_gives_the_bucketed_stream():
         if a.argmax().item() != b.argmax().item():
             top2 = a.flatten().topk(2).values
             assert (top2[0] - top2[1]).item() <= 4e-2, step
+
+
+def test_speculative_greedy_is_the_target_greedy_stream():
+    """Greedy speculative decoding is exact: with a draft runner proposing four tokens per round
+    and the target verifying them (spec_round, the reference's _spec_round), the stream equals the
+    target's own greedy stream. A draft on the same weights accepts whole rounds (the all-accepted
+    branch, with the draft's continuity decode); an unrelated draft is rejected early. Verify scores
+    five rows through the multi-row projections and decode one row through the GEMV, so at a step
+    whose top-2 margin is a numerical near-tie the two streams may part; there the target's
+    teacher-forced margin must be <= 4e-2 and the speculative token one of its top two."""
+    from solort_b200.runner import GraphQwen3Runner, speculative_greedy
+
+    model = _model(3, 32, 8, 1024, 2048, 4096, seed=3)
+    other = _model(2, 32, 8, 1024, 2048, 4096, seed=11)
+    prompt = torch.randint(0, 4096, (60,), generator=torch.Generator().manual_seed(8)).cuda()
+    steps, k = 32, 4
+    with torch.no_grad():
+        greedy = GraphQwen3Runner(model, 256).greedy(prompt, steps)
+        forced = _teacher_forced(GraphQwen3Runner(model, 256), prompt, greedy)
+        for draft_model, full_rounds in ((model, True), (other, False)):
+            spec, accepted = speculative_greedy(GraphQwen3Runner(model, 256),
+                                                GraphQwen3Runner(draft_model, 256), prompt,
+                                                steps, k)
+            assert len(spec) == steps + 1
+            if full_rounds:
+                assert any(a == k for a in accepted), accepted
+            else:
+                assert any(a < k for a in accepted), accepted
+            i = _first_divergence(spec, greedy)
+            if i is not None:
+                top2 = forced[i].flatten().topk(2)
+                assert (top2.values[0] - top2.values[1]).item() <= 4e-2, (i, accepted)
+                assert spec[i] in top2.indices.tolist(), i
