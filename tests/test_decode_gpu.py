@@ -52,6 +52,21 @@ def test_decode_static_nhd(nh, nkv, L):
     assert ops.device_status() == 0
 
 
+def test_decode_full_size_config5_one_gpu():
+    """BASELINE config 5 on one GPU: one query over 131072 keys with the default split plan, against
+    the same fp32 attention evaluated on the device (the host oracle is slow at this size)."""
+    ops = _ops()
+    L = 131072
+    q, k, v = _static_case(5, 32, 8, L, 1)
+    dq, dk, dv = q.cuda(), k.cuda(), v.cuda()
+    qpos = torch.tensor([L - 1], dtype=torch.int64, device="cuda")
+    out = ops.gqa_decode(dq[None], dk, dv, qpos, stable_prefix=True)
+    ref, _ = A.attention_fp32(dq, dk, dv, 128**-0.5, L - 1)
+    torch.cuda.synchronize()
+    assert_close(out[0].cpu(), ref.cpu(), "decode L=131072")
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("splits", [1, 2, 3, 17])
 def test_decode_forced_splits(splits):
     ops = _ops()

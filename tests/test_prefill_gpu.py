@@ -109,3 +109,18 @@ def test_prefill_ping_pong_over_cache(q_len, kv_len, causal):
     torch.cuda.synchronize()
     _close(out, ref, f"ping-pong q={q_len} kv={kv_len} causal={causal}")
     assert ops.device_status() == 0
+
+
+def test_prefill_full_size_config3():
+    """BASELINE config 3 at its largest size (T = 4096, 32 query / 8 KV heads), against the same
+    fp32 attention evaluated on the device (too slow on the host at this size)."""
+    from solort_b200 import ops
+
+    T = 4096
+    q, k, v = A.make_attention_inputs(4242, 32, 8, 128, T, T, 0)
+    dq, dk, dv = q.cuda(), k.cuda(), v.cuda()
+    out = ops.gqa_prefill(dq, dk, dv)
+    ref, _ = A.attention_fp32(dq, dk, dv, 128 ** -0.5, 0)
+    torch.cuda.synchronize()
+    _close(out, ref, "prefill T=4096 32/8")
+    assert ops.device_status() == 0
