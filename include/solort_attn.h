@@ -25,6 +25,8 @@
  *   solort_attn_decode with a block table (paged KV, NHD pages [pages, 2, P, nkv, hd]):
  *       src/solort/backends/transformers_flashinfer.py:95-129  (AttentionInterface decode/prefill)
  *       src/solort/cache/kv_cache.py:86-100,136-149            (page layout, slot = bt[p//P]*P+p%P)
+ *   solort_attn_kv_store (slot-mapped K/V mirror into the paged arena):
+ *       src/solort/cache/kv_cache.py:191-235, called from transformers_flashinfer.py:93,205-220
  *   solort_attn_decode with out_f32/lse_out + solort_attn_lse_merge, and
  *   solort_attn_decode_exchange + solort_attn_exchange_merge:
  *       no counterpart (the reference is single-GPU); sequence-sharded long-context decode.
@@ -39,7 +41,7 @@
 extern "C" {
 #endif
 
-#define SOLORT_ATTN_ABI_VERSION 2
+#define SOLORT_ATTN_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SOLORT_API __attribute__((visibility("default")))
@@ -142,10 +144,11 @@ SOLORT_API int solort_attn_decode(const SolortDecodeArgs* args, void* stream);
  *  - Limit: calls whose split partials need more than 4 MiB (solort_attn_decode_workspace_size)
  *    are rejected with SOLORT_ERR_SCRATCH_LIMIT; use solort_attn_decode with a workspace for them.
  *    Decode of one sequence with 32 query heads (37 splits) needs about 0.6 MiB.
- *  - The array is allocated once per GPU when the library's device code loads, and stays until the
- *    process exits.
- *  - The first call on each device looks up the array's device address (with that device current);
- *    make that first call before any stream capture on that device.
+ *  - The array exists on a GPU from the moment the library's device code is loaded in that GPU's
+ *    context (at the latest, the first call on it) until that context is destroyed.
+ *  - Each call looks up the array's device address on the current device. The first call in a
+ *    device context loads the device code, which a stream capture does not allow: make that first
+ *    call before any stream capture on that device.
  *  - All calls on a GPU share the array and it keeps the last call's contents. Nothing in it needs
  *    to start at zero (a call writes every part it reads), but calls that overlap on the GPU, for
  *    example on two streams, race on it: serialise them.
@@ -299,6 +302,35 @@ typedef struct SolortPrologueArgs {
 SOLORT_API int solort_attn_qk_norm_rope_append(const SolortPrologueArgs* args, void* stream);
 
 /*
+ * Slot-mapped store of num_tokens tokens' K and V rows into a paged arena: token i goes to
+ * physical slot slots[i] = page * page_size + row. Replaces the per-token Python loop of
+ * PagedKVCache.store_layer_tokens (src/solort/cache/kv_cache.py:191-235), which the HF bridge
+ * calls to mirror each layer's K / V (src/solort/backends/transformers_flashinfer.py:93,205-220).
+ *   key, value  token i, kv head h at key + i*src_stride_token + h*src_stride_head (bf16, the 128
+ *               dims contiguous); for the HF layout [1, nkv, kv, 128] pass the last num_tokens
+ *               tokens' base with src_stride_token = 128 and src_stride_head = kv * 128
+ *   slots       int64 [num_tokens] on the device
+ *   k_pages, v_pages  row (page p, row r, head h) at + p*dst_stride_page + r*dst_stride_token +
+ *               h*dst_stride_head; for SoloRT's arena [pages, 2, P, nkv, 128]: v_pages = k_pages +
+ *               P*nkv*128, dst_stride_page = 2*P*nkv*128
+ * Copies are bit-exact. A slot outside [0, num_pages * page_size) is skipped and sets bit 4 of the
+ * device status. Pointers 16-byte aligned, strides multiples of 8 elements.
+ */
+typedef struct SolortKVStoreArgs {
+  const void* key;
+  const void* value;
+  int64_t src_stride_token, src_stride_head;
+  int32_t num_tokens, num_kv_heads, head_dim;
+  const int64_t* slots;
+  void* k_pages;
+  void* v_pages;
+  int64_t dst_stride_page, dst_stride_token, dst_stride_head;
+  int32_t page_size, num_pages;
+} SolortKVStoreArgs;
+
+SOLORT_API int solort_attn_kv_store(const SolortKVStoreArgs* args, void* stream);
+
+/*
  * Layer glue of the runner's step (decode, verify or prefill) around the attention.
  * solort_attn_add_rmsnorm: per row, x_out = x + delta (bf16, when delta != NULL; x_out may be x),
  * then h_out = RMSNorm(x_out) * weight: fp32 x * rsqrt(mean(x^2) + eps), times the weight, cast to
@@ -372,7 +404,7 @@ SOLORT_API int solort_attn_gemv(const SolortGemvArgs* args, void* stream);
  * its time limit and the kernel returned without writing its output; bit 1: a tensor-memory
  * allocation wait hit its limit; bit 2: a kernel found its shared memory misaligned and returned
  * without writing; bit 3: an exchange merge waited a second for a peer's partial and left the
- * row unwritten). */
+ * row unwritten; bit 4: solort_attn_kv_store met a slot outside the arena and skipped it). */
 SOLORT_API int solort_attn_device_status(unsigned* flags);
 
 SOLORT_API const char* solort_attn_status_string(int code);

@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "solort_attn_add_rmsnorm",
     "solort_attn_silu_mul",
     "solort_attn_gemv",
+    "solort_attn_kv_store",
 )
 
 MAX_RANKS = 8  # SOLORT_MAX_RANKS
@@ -193,6 +194,22 @@ class SolortGemvArgs(ctypes.Structure):
     ]
 
 
+class SolortKVStoreArgs(ctypes.Structure):
+    """Mirror of ``SolortKVStoreArgs`` in ``include/solort_attn.h``."""
+
+    _fields_ = [
+        ("key", c_vp),
+        ("value", c_vp),
+        ("src_stride_token", c_i64), ("src_stride_head", c_i64),
+        ("num_tokens", c_i32), ("num_kv_heads", c_i32), ("head_dim", c_i32),
+        ("slots", c_vp),
+        ("k_pages", c_vp),
+        ("v_pages", c_vp),
+        ("dst_stride_page", c_i64), ("dst_stride_token", c_i64), ("dst_stride_head", c_i64),
+        ("page_size", c_i32), ("num_pages", c_i32),
+    ]
+
+
 _LIB: ctypes.CDLL | None = None
 
 
@@ -253,6 +270,8 @@ def _optional_symbols(lib: ctypes.CDLL) -> None:
     lib.solort_attn_silu_mul.restype = ctypes.c_int
     lib.solort_attn_gemv.argtypes = [P(SolortGemvArgs), c_vp]
     lib.solort_attn_gemv.restype = ctypes.c_int
+    lib.solort_attn_kv_store.argtypes = [P(SolortKVStoreArgs), c_vp]
+    lib.solort_attn_kv_store.restype = ctypes.c_int
 
 
 class SolortPrefillArgs(ctypes.Structure):

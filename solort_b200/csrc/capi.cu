@@ -5,6 +5,7 @@ namespace solort {
 int read_decode_status(unsigned* flags);
 int read_prefill_status(unsigned* flags);
 int read_exchange_status(unsigned* flags);
+int read_store_status(unsigned* flags);
 }  // namespace solort
 
 extern "C" int solort_attn_abi_version(void) { return SOLORT_ATTN_ABI_VERSION; }
@@ -44,6 +45,8 @@ extern "C" int solort_attn_device_status(unsigned* flags) {
   rc = solort::read_decode_status(flags);
   if (rc != SOLORT_OK) return rc;
   rc = solort::read_exchange_status(flags);
+  if (rc != SOLORT_OK) return rc;
+  rc = solort::read_store_status(flags);
   if (rc != SOLORT_OK) return rc;
   return solort::read_prefill_status(flags);
 }

@@ -24,6 +24,7 @@
 // (src/solort/model/cuda_graph_executor.py:168,180-184: keys 0..pos visible), verify (:250: query
 // i at vpos0+i sees keys <= vpos0+i) and the paged addressing of src/solort/cache/kv_cache.py:
 // 136-149 (slot = block_table[pos // P] * P + pos % P).
+#include <atomic>
 #include <math.h>
 #include <string.h>
 
@@ -794,19 +795,19 @@ inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStr
 template <int MT, bool PAGED>
 int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, dim3 grid,
                   size_t smem, cudaStream_t stream) {
-  static unsigned configured = 0;  // one bit per device ordinal < 32
+  static std::atomic<unsigned> configured{0};  // one bit per device ordinal < 32
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
   const size_t max_smem = kSmemPerCta;
   if (smem > max_smem) return SOLORT_ERR_UNSUPPORTED;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (dev >= 32 || !(configured.load(std::memory_order_acquire) & (1u << dev))) {
     if (cudaFuncSetAttribute(decode_kernel<MT, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(max_smem)) != cudaSuccess ||
         cudaFuncSetAttribute(decode_kernel<MT, PAGED>,
                              cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return SOLORT_ERR_CUDA;
-    if (dev < 32) configured |= 1u << dev;
+    if (dev < 32) configured.fetch_or(1u << dev, std::memory_order_release);
   }
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(grid, dim3(Shape<MT>::kThreads), smem, stream, attr);
@@ -1128,21 +1129,18 @@ constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB of split parti
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 // Device address of g_static_scratch on the current device. In host code the array's name is only
-// a host-side stand-in, so the address is looked up once per device, with that device current, and
-// cached.
+// a host-side stand-in, so the address is looked up with the device current. The lookup runs on
+// every call rather than being cached per device ordinal: once the library's device code is loaded
+// it is a table read, and a context that was destroyed and recreated (cudaDeviceReset) may place
+// the array elsewhere, which a cached address would miss. The first lookup in a context loads the
+// device code, which must not happen inside a stream capture.
 int static_scratch_address(void** out) {
-  static std::mutex mu;
-  static void* addr[64] = {};
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SOLORT_ERR_NO_DEVICE;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr)
-      return SOLORT_ERR_CUDA;
-    addr[dev] = p;
-  }
-  *out = addr[dev];
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return SOLORT_ERR_NO_DEVICE;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || p == nullptr)
+    return SOLORT_ERR_CUDA;
+  *out = p;
   return SOLORT_OK;
 }
 
@@ -1156,7 +1154,7 @@ extern "C" int solort_attn_decode_static_scratch(const SolortDecodeArgs* a, void
   if (rc != SOLORT_OK) return rc;
   if (need > kStaticScratchBytes) return SOLORT_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
-  rc = static_scratch_address(&scratch);  // the first call on a device does this set-up
+  rc = static_scratch_address(&scratch);  // the first call in a device context loads the array
   if (rc != SOLORT_OK) return rc;
   SolortDecodeArgs with_scratch = *a;
   with_scratch.workspace = scratch;

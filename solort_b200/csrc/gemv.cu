@@ -23,6 +23,7 @@
 // cannot overlap the kernels before and after it), a double-buffered register pipeline (half the
 // resident warps), ten loads per lane in flight, and the whole MLP as one launch with a grid
 // barrier between gate_up and down (the barrier cost more than the kernel boundary).
+#include <atomic>
 #include <math.h>
 
 #include <algorithm>
@@ -271,14 +272,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_kernel(const Params
 
 template <int T, int S>
 int launch(const Params& p, size_t smem, int grid, cudaStream_t stream) {
-  static unsigned configured = 0;
+  static std::atomic<unsigned> configured{0};  // one bit per device ordinal < 32
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (dev >= 32 || !(configured.load(std::memory_order_acquire) & (1u << dev))) {
     if (cudaFuncSetAttribute(gemv_kernel<T, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kMaxStageBytes) != cudaSuccess)
       return SOLORT_ERR_CUDA;
-    if (dev < 32) configured |= 1u << dev;
+    if (dev < 32) configured.fetch_or(1u << dev, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));

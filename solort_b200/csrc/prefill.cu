@@ -23,6 +23,7 @@
 // cuda_graph_executor.py:124-130) and the HF bridge's bottom-right causal alignment when q_len <
 // kv_len (src/solort/backends/transformers_flashinfer.py:182-193): query i sees keys
 // j <= kv_len - q_len + i.
+#include <atomic>
 #include <math.h>
 
 #include "common.cuh"
@@ -955,16 +956,16 @@ extern "C" int solort_attn_prefill(const SolortPrefillArgs* a, void* stream_v) {
                        a->num_qo_heads;
   if (grid > (1ll << 31) - 1) return SOLORT_ERR_UNSUPPORTED;
   if (ping_pong && di.max_smem_optin < pp::kSmemBytes) return SOLORT_ERR_UNSUPPORTED;
-  static unsigned configured = 0;
+  static std::atomic<unsigned> configured{0};  // one bit per device ordinal < 32
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
-  if (dev >= 32 || !(configured & (1u << dev))) {
+  if (dev >= 32 || !(configured.load(std::memory_order_acquire) & (1u << dev))) {
     if (cudaFuncSetAttribute(prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kSmemBytes) != cudaSuccess ||
         cudaFuncSetAttribute(pp::prefill_pp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pp::kSmemBytes) != cudaSuccess)
       return SOLORT_ERR_CUDA;
-    if (dev < 32) configured |= 1u << dev;
+    if (dev < 32) configured.fetch_or(1u << dev, std::memory_order_release);
   }
   if (ping_pong)
     pp::prefill_pp_kernel<<<static_cast<unsigned>(grid), kThreads, pp::kSmemBytes,

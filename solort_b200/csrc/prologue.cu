@@ -21,6 +21,9 @@
 namespace solort {
 namespace pro {
 
+constexpr unsigned kDevErrSlotRange = 1u << 4;  // solort_attn_kv_store skipped a slot past the arena
+__device__ unsigned g_store_status;
+
 constexpr int kHD = 128;
 constexpr int kWarpsPerCta = 8;
 
@@ -196,5 +199,115 @@ extern "C" int solort_attn_qk_norm_rope_append(const SolortPrologueArgs* a, void
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, pro::prologue_kernel, p) != cudaSuccess) return SOLORT_ERR_CUDA;
+  return launch_status();
+}
+
+// ------------------------------------------------------------------------------------------------
+// Slot-mapped KV store (the HF bridge's mirror into SoloRT's paged arena). The reference writes
+// one token at a time from Python (src/solort/cache/kv_cache.py:230-235: k_cache[layer, page,
+// offset].copy_(k_tokens[i]) for each slot); here one warp moves one (token, head) row of K and
+// one of V, 256 bytes each as a 16-byte load and store per lane over 16 lanes.
+// ------------------------------------------------------------------------------------------------
+namespace solort {
+namespace pro {
+
+struct StoreParams {
+  const bf16* key;
+  const bf16* value;
+  int64_t src_st, src_sh;
+  int t, nkv;
+  const int64_t* slots;
+  bf16* k_pages;
+  bf16* v_pages;
+  int64_t dst_sp, dst_st, dst_sh;
+  int page_shift, page_size;
+  long long slot_limit;  // num_pages * page_size
+};
+
+__global__ void __launch_bounds__(kWarpsPerCta * 32) kv_store_kernel(const StoreParams p) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int lane = threadIdx.x & 31;
+  const int w = blockIdx.x * kWarpsPerCta + (threadIdx.x >> 5);
+  if (w >= p.t * p.nkv) return;
+  const int tok = w / p.nkv, h = w % p.nkv;
+  const long long slot = p.slots[tok];
+  if (slot < 0 || slot >= p.slot_limit) {
+    if (lane == 0) atomicOr(&g_store_status, kDevErrSlotRange);
+    return;
+  }
+  const long long page = slot >> p.page_shift;
+  const int row = static_cast<int>(slot & (p.page_size - 1));
+  const int64_t dst = page * p.dst_sp + row * p.dst_st + h * p.dst_sh;
+  const int64_t src = tok * p.src_st + h * p.src_sh;
+  // lanes 0-15 move the K row, lanes 16-31 the V row: 16 lanes x 16 bytes = 128 bf16 each
+  const int part = lane & 15;
+  const bf16* from = (lane < 16 ? p.key : p.value) + src + part * 8;
+  bf16* to = (lane < 16 ? p.k_pages : p.v_pages) + dst + part * 8;
+  *reinterpret_cast<uint4*>(to) = *reinterpret_cast<const uint4*>(from);
+}
+
+}  // namespace pro
+
+int read_store_status(unsigned* flags) {
+  unsigned v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, pro::g_store_status, sizeof(v)) != cudaSuccess)
+    return SOLORT_ERR_CUDA;
+  if (v && cudaMemcpyToSymbol(pro::g_store_status, &zero, sizeof(zero)) != cudaSuccess)
+    return SOLORT_ERR_CUDA;
+  *flags |= v;
+  return SOLORT_OK;
+}
+
+}  // namespace solort
+
+extern "C" int solort_attn_kv_store(const SolortKVStoreArgs* a, void* stream) {
+  if (!a || !a->key || !a->value || !a->slots || !a->k_pages || !a->v_pages)
+    return SOLORT_ERR_INVALID_ARGUMENT;
+  if (a->head_dim != pro::kHD) return SOLORT_ERR_UNSUPPORTED;
+  if (a->num_tokens < 0 || a->num_kv_heads <= 0 || a->num_pages <= 0)
+    return SOLORT_ERR_INVALID_ARGUMENT;
+  const int P = a->page_size;
+  if (P < 1 || (P & (P - 1)) != 0) return SOLORT_ERR_INVALID_ARGUMENT;
+  // 16-byte vector accesses: pointers 16-aligned, strides multiples of 8 elements.
+  const int64_t strides = a->src_stride_token | a->src_stride_head | a->dst_stride_page |
+                          a->dst_stride_token | a->dst_stride_head;
+  if ((strides & 7) || !aligned(a->key, 16) || !aligned(a->value, 16) ||
+      !aligned(a->k_pages, 16) || !aligned(a->v_pages, 16) || !aligned(a->slots, 8))
+    return SOLORT_ERR_INVALID_ARGUMENT;
+  if (a->num_tokens == 0) return SOLORT_OK;
+  DeviceInfo di;
+  int rc = current_device_info(&di);
+  if (rc != SOLORT_OK) return rc;
+  const int64_t warps = static_cast<int64_t>(a->num_tokens) * a->num_kv_heads;
+  if (warps > (1ll << 30)) return SOLORT_ERR_UNSUPPORTED;
+  pro::StoreParams p{};
+  p.key = static_cast<const bf16*>(a->key);
+  p.value = static_cast<const bf16*>(a->value);
+  p.src_st = a->src_stride_token;
+  p.src_sh = a->src_stride_head;
+  p.t = a->num_tokens;
+  p.nkv = a->num_kv_heads;
+  p.slots = a->slots;
+  p.k_pages = static_cast<bf16*>(a->k_pages);
+  p.v_pages = static_cast<bf16*>(a->v_pages);
+  p.dst_sp = a->dst_stride_page;
+  p.dst_st = a->dst_stride_token;
+  p.dst_sh = a->dst_stride_head;
+  int shift = 0;
+  while ((1 << shift) < P) ++shift;
+  p.page_shift = shift;
+  p.page_size = P;
+  p.slot_limit = static_cast<long long>(a->num_pages) * P;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((warps + pro::kWarpsPerCta - 1) / pro::kWarpsPerCta));
+  cfg.blockDim = dim3(pro::kWarpsPerCta * 32);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, pro::kv_store_kernel, p) != cudaSuccess) return SOLORT_ERR_CUDA;
   return launch_status();
 }

@@ -15,145 +15,32 @@ import math
 
 import torch
 
-from solort_b200 import _lib
+from solort_b200 import _calls, _lib
+from solort_b200 import torch_ops  # noqa: F401  (registers torch.ops.solort_attn.*)
+from solort_b200._calls import (  # noqa: F401  (re-exported for callers of the C-ABI helpers)
+    HEAD_DIM, _check_cuda, _decode_args, _ptr, _run_decode, _static_kv, _stream, _stream_at,
+    decode_workspace_bytes)
 
-HEAD_DIM = 128
-
-
-def _ptr(t: torch.Tensor | None) -> int | None:
-    return None if t is None else t.data_ptr()
-
-
-# torch's raw getter of the current stream handle: the same value as
-# ``torch.cuda.current_stream(device).cuda_stream`` (the capture stream while a graph is captured),
-# without building a Stream object, which costs ~2 us of host time per call.
-_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_OPS = torch.ops.solort_attn
+_NO_WORKSPACE: dict[torch.device, torch.Tensor] = {}
 
 
-def _stream_at(index: int) -> int:
-    if _RAW_STREAM is not None:
-        return _RAW_STREAM(index)
-    return torch.cuda.current_stream(index).cuda_stream
+def _empty_workspace(device: torch.device) -> torch.Tensor:
+    """A zero-byte tensor standing for "no workspace" (calls whose split plan needs none)."""
+    ws = _NO_WORKSPACE.get(device)
+    if ws is None:
+        ws = _NO_WORKSPACE[device] = torch.empty(0, dtype=torch.uint8, device=device)
+    return ws
 
 
-def _stream(device: torch.device) -> int:
-    return _stream_at(device.index if device.index is not None else torch.cuda.current_device())
-
-
-def _check_cuda(name: str, t: torch.Tensor, dtype: torch.dtype | None = None) -> None:
-    if not isinstance(t, torch.Tensor) or not t.is_cuda:
-        raise RuntimeError(f"{name} must be a CUDA tensor")
-    if dtype is not None and t.dtype != dtype:
-        raise RuntimeError(f"{name} must be {dtype}, got {t.dtype}")
-
-
-def _decode_args(
-    q: torch.Tensor,
-    k: torch.Tensor,
-    v: torch.Tensor,
-    q_pos: torch.Tensor,
-    *,
-    stride_token: int,
-    stride_head: int,
-    stride_page: int,
-    kv_capacity: int,
-    num_kv_heads: int,
-    block_table: torch.Tensor | None,
-    page_size: int,
-    num_pages: int,
-    scale: float | None,
-    max_kv_len: int,
-    out: torch.Tensor | None,
-    out_f32: torch.Tensor | None,
-    lse_out: torch.Tensor | None,
-    q_lens: torch.Tensor | None,
-    kv_pos_offset: int,
-    num_splits: int,
-    stable_prefix: bool = False,
-) -> _lib.SolortDecodeArgs:
-    _check_cuda("q", q, torch.bfloat16)
-    if q.dim() != 4 or q.shape[-1] != HEAD_DIM or q.stride(-1) != 1:
-        raise RuntimeError("q must be [batch, q_len, num_qo_heads, 128] with a contiguous head dim")
-    _check_cuda("q_pos", q_pos, torch.int64)
-    B, T, H, D = q.shape
-    a = _lib.SolortDecodeArgs()
-    a.q = q.data_ptr()
-    a.q_stride_batch, a.q_stride_token, a.q_stride_head = q.stride(0), q.stride(1), q.stride(2)
-    if out is not None:
-        a.out = out.data_ptr()
-        a.out_stride_batch, a.out_stride_token, a.out_stride_head = out.stride(0), out.stride(1), out.stride(2)
-    a.out_f32 = _ptr(out_f32)
-    a.lse_out = _ptr(lse_out)
-    a.k, a.v = k.data_ptr(), v.data_ptr()
-    a.kv_stride_token, a.kv_stride_head, a.kv_stride_page = stride_token, stride_head, stride_page
-    a.kv_capacity = kv_capacity
-    a.block_table = _ptr(block_table)
-    a.block_table_stride = block_table.stride(0) if block_table is not None else 0
-    a.page_size = page_size
-    a.num_pages = num_pages
-    a.q_pos = q_pos.data_ptr()
-    a.q_lens = _ptr(q_lens)
-    a.kv_pos_offset = int(kv_pos_offset)
-    a.batch, a.q_len, a.num_qo_heads, a.num_kv_heads, a.head_dim = B, T, H, num_kv_heads, D
-    a.max_kv_len = int(max_kv_len)
-    a.scale = float(D ** -0.5 if scale is None else scale)
-    a.num_splits = int(num_splits)
-    a.flags = _lib.DECODE_STABLE_PREFIX if stable_prefix else 0
-    return a
-
-
-def _run_decode(a: _lib.SolortDecodeArgs, device: torch.device, workspace: torch.Tensor | None):
-    lib = _lib.load()
-    need = ctypes.c_size_t(0)
-    _lib.check(lib.solort_attn_decode_workspace_size(ctypes.byref(a), ctypes.byref(need)),
-               "solort_attn_decode_workspace_size")
-    if need.value > 0:
-        if workspace is None:
-            workspace = torch.empty(need.value, dtype=torch.uint8, device=device)
-        a.workspace = workspace.data_ptr()
-        a.workspace_bytes = workspace.numel() * workspace.element_size()
-    _lib.check(lib.solort_attn_decode(ctypes.byref(a), ctypes.c_void_p(_stream(device))),
-               "solort_attn_decode")
-
-
-def _static_kv(k_cache: torch.Tensor, v_cache: torch.Tensor, kv_layout: str):
-    _check_cuda("k_cache", k_cache, torch.bfloat16)
-    _check_cuda("v_cache", v_cache, torch.bfloat16)
-    if k_cache.shape != v_cache.shape or k_cache.stride() != v_cache.stride():
-        raise RuntimeError("k_cache and v_cache must have the same shape and strides")
-    if k_cache.dim() != 3 or k_cache.shape[-1] != HEAD_DIM or k_cache.stride(-1) != 1:
-        raise RuntimeError("static KV must be 3-D with a contiguous head dim of 128")
-    if kv_layout == "NHD":
-        cap, nkv = k_cache.shape[0], k_cache.shape[1]
-        st, sh = k_cache.stride(0), k_cache.stride(1)
-    elif kv_layout == "HND":
-        nkv, cap = k_cache.shape[0], k_cache.shape[1]
-        sh, st = k_cache.stride(0), k_cache.stride(1)
-    else:
-        raise RuntimeError(f"kv_layout must be 'NHD' or 'HND', got {kv_layout!r}")
-    return cap, nkv, st, sh
-
-
-def decode_workspace_bytes(
-    batch: int, q_len: int, num_qo_heads: int, num_kv_heads: int, max_kv_len: int,
-    *, kv_capacity: int | None = None, page_size: int = 0, num_splits: int = 0,
-) -> int:
-    """Workspace bytes a decode call with these sizes needs on the current device."""
-    a = _lib.SolortDecodeArgs()
-    a.batch, a.q_len, a.num_qo_heads, a.num_kv_heads, a.head_dim = (
-        batch, q_len, num_qo_heads, num_kv_heads, HEAD_DIM)
-    a.max_kv_len = max_kv_len
-    a.kv_capacity = kv_capacity if kv_capacity is not None else max_kv_len
-    if page_size:
-        a.block_table = 1  # any non-null pointer selects the paged plan
-        a.page_size = page_size
-        a.num_pages = 1
-    a.num_splits = num_splits
-    need = ctypes.c_size_t(0)
-    _lib.check(_lib.load().solort_attn_decode_workspace_size(ctypes.byref(a), ctypes.byref(need)),
-               "solort_attn_decode_workspace_size")
-    return int(need.value)
-
+def _workspace_for(a: _lib.SolortDecodeArgs, device: torch.device,
+                   workspace: torch.Tensor | None) -> torch.Tensor:
+    if workspace is not None:
+        return workspace
+    need = _calls.decode_workspace_needed(a)
+    if need == 0:
+        return _empty_workspace(device)
+    return torch.empty(need, dtype=torch.uint8, device=device)
 
 def gqa_decode(
     q: torch.Tensor,
@@ -170,7 +57,8 @@ def gqa_decode(
     num_splits: int = 0,
     stable_prefix: bool = False,
 ) -> torch.Tensor:
-    """GQA attention of ``q [B, q_len, nh, 128]`` against one layer's static KV buffer.
+    """GQA attention of ``q [B, q_len, nh, 128]`` against one layer's static KV buffer, through
+    ``torch.ops.solort_attn.gqa_decode``.
 
     ``k_cache``/``v_cache`` are ``[max_len, nkv, 128]`` (``kv_layout="NHD"``, the reference's
     ``kc[li]``/``vc[li]`` of ``cuda_graph_executor.py:67-69``) or ``[nkv, max_len, 128]``
@@ -179,21 +67,21 @@ def gqa_decode(
     (``:250,261-263``) with ``q_len == K + 1``. ``max_kv_len`` bounds the keys read (the decode
     bucket ``bound``); it defaults to the buffer length. ``stable_prefix``: ``q_pos`` and the keys
     below it were written before the kernel launched just before this call (earlier steps), so
-    their loads may start during that kernel's tail (``SOLORT_DECODE_STABLE_PREFIX``).
+    their loads may start during that kernel's tail (``SOLORT_DECODE_STABLE_PREFIX``). ``out`` and
+    ``workspace`` are allocated when not given (pass both to capture the call in a CUDA graph).
     """
-    cap, nkv, st, sh = _static_kv(k_cache, v_cache, kv_layout)
-    if q_pos.numel() != q.shape[0]:
-        raise RuntimeError(f"q_pos has {q_pos.numel()} entries for batch {q.shape[0]}")
+    cap, nkv, _, _ = _static_kv(k_cache, v_cache, kv_layout)
+    _check_cuda("q", q, torch.bfloat16)
     if out is None:
         out = torch.empty_like(q)
-    a = _decode_args(
-        q, k_cache, v_cache, q_pos, stride_token=st, stride_head=sh, stride_page=0,
-        kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
-        scale=scale, max_kv_len=max_kv_len or cap, out=out, out_f32=None, lse_out=None,
-        q_lens=q_lens, kv_pos_offset=0, num_splits=num_splits, stable_prefix=stable_prefix)
-    _run_decode(a, q.device, workspace)
+    if workspace is None:
+        need = decode_workspace_bytes(q.shape[0], q.shape[1], q.shape[2], nkv, max_kv_len or cap,
+                                      kv_capacity=cap, num_splits=num_splits)
+        workspace = (torch.empty(need, dtype=torch.uint8, device=q.device) if need
+                     else _empty_workspace(q.device))
+    _OPS.gqa_decode(q, k_cache, v_cache, q_pos, out, workspace, kv_layout, scale,
+                    int(max_kv_len or 0), q_lens, int(num_splits), bool(stable_prefix))
     return out
-
 
 class DecodeCall:
     """A prepared ``gqa_decode`` on fixed buffers: arguments are checked and packed once, and
@@ -293,22 +181,25 @@ def gqa_decode_partial(
     num_splits: int = 0,
 ):
     """Like ``gqa_decode`` over one shard of the keys, returning the partial
-    ``(O fp32 [B, q_len, nh, 128], LSE fp32 [B, q_len, nh])`` for ``lse_merge``. Local key ``t``
-    of the shard sits at absolute position ``kv_pos_offset + t``."""
-    cap, nkv, st, sh = _static_kv(k_cache, v_cache, kv_layout)
+    ``(O fp32 [B, q_len, nh, 128], LSE fp32 [B, q_len, nh])`` for ``lse_merge``
+    (``torch.ops.solort_attn.gqa_decode_partial``). Local key ``t`` of the shard sits at absolute
+    position ``kv_pos_offset + t``."""
+    cap, nkv, _, _ = _static_kv(k_cache, v_cache, kv_layout)
+    _check_cuda("q", q, torch.bfloat16)
     B, T, H, D = q.shape
     if out_f32 is None:
         out_f32 = torch.empty(B, T, H, D, dtype=torch.float32, device=q.device)
     if lse_out is None:
         lse_out = torch.empty(B, T, H, dtype=torch.float32, device=q.device)
-    a = _decode_args(
-        q, k_cache, v_cache, q_pos, stride_token=st, stride_head=sh, stride_page=0,
-        kv_capacity=cap, num_kv_heads=nkv, block_table=None, page_size=0, num_pages=0,
-        scale=scale, max_kv_len=max_kv_len or cap, out=None, out_f32=out_f32, lse_out=lse_out,
-        q_lens=None, kv_pos_offset=kv_pos_offset, num_splits=num_splits)
-    _run_decode(a, q.device, workspace)
+    if workspace is None:
+        need = decode_workspace_bytes(B, T, H, nkv, max_kv_len or cap, kv_capacity=cap,
+                                      num_splits=num_splits)
+        workspace = (torch.empty(need, dtype=torch.uint8, device=q.device) if need
+                     else _empty_workspace(q.device))
+    _OPS.gqa_decode_partial(q, k_cache, v_cache, q_pos, out_f32, lse_out, workspace,
+                            int(kv_pos_offset), kv_layout, scale, int(max_kv_len or 0),
+                            int(num_splits))
     return out_f32, lse_out
-
 
 def gqa_decode_paged(
     q: torch.Tensor,
@@ -324,7 +215,8 @@ def gqa_decode_paged(
     num_splits: int = 0,
     stable_prefix: bool = False,
 ) -> torch.Tensor:
-    """GQA attention against one layer of SoloRT's paged arena.
+    """GQA attention against one layer of SoloRT's paged arena
+    (``torch.ops.solort_attn.gqa_decode_paged``).
 
     ``kv_pages [num_pages, 2, P, nkv, 128]`` is one layer of ``PagedKVCache.kv_cache``
     (``kv_cache.py:86-100``); ``block_table [B, max_pages]`` int32 holds physical page ids as the
@@ -334,30 +226,18 @@ def gqa_decode_paged(
     the keys any sequence may see; ``stable_prefix`` as in ``gqa_decode`` (it also covers the
     block table).
     """
-    _check_cuda("kv_pages", kv_pages, torch.bfloat16)
-    _check_cuda("block_table", block_table, torch.int32)
-    if kv_pages.dim() != 5 or kv_pages.shape[1] != 2 or kv_pages.shape[-1] != HEAD_DIM:
-        raise RuntimeError("kv_pages must be [num_pages, 2, page_size, nkv, 128]")
-    if kv_pages.stride(-1) != 1:
-        raise RuntimeError("kv_pages must have a contiguous head dim")
-    if block_table.dim() != 2 or block_table.stride(1) != 1 or block_table.shape[0] != q.shape[0]:
-        raise RuntimeError("block_table must be [batch, max_pages] with contiguous rows")
-    num_pages, _, P, nkv, _ = kv_pages.shape
-    if max_kv_len > block_table.shape[1] * P:
-        raise RuntimeError("max_kv_len exceeds the pages a block-table row can hold")
+    _check_cuda("q", q, torch.bfloat16)
     if out is None:
         out = torch.empty_like(q)
-    k = kv_pages[:, 0]
-    v = kv_pages[:, 1]
-    a = _decode_args(
-        q, k, v, q_pos, stride_token=kv_pages.stride(2), stride_head=kv_pages.stride(3),
-        stride_page=kv_pages.stride(0), kv_capacity=0, num_kv_heads=nkv,
-        block_table=block_table, page_size=P, num_pages=num_pages, scale=scale,
-        max_kv_len=max_kv_len, out=out, out_f32=None, lse_out=None, q_lens=q_lens,
-        kv_pos_offset=0, num_splits=num_splits, stable_prefix=stable_prefix)
-    _run_decode(a, q.device, workspace)
+    if workspace is None:
+        need = decode_workspace_bytes(q.shape[0], q.shape[1], q.shape[2], kv_pages.shape[3],
+                                      max_kv_len, kv_capacity=0, page_size=kv_pages.shape[2],
+                                      num_splits=num_splits)
+        workspace = (torch.empty(need, dtype=torch.uint8, device=q.device) if need
+                     else _empty_workspace(q.device))
+    _OPS.gqa_decode_paged(q, kv_pages, block_table, q_pos, out, workspace, int(max_kv_len), scale,
+                          q_lens, int(num_splits), bool(stable_prefix))
     return out
-
 
 def lse_merge(
     o_parts: torch.Tensor,
@@ -368,37 +248,22 @@ def lse_merge(
 ):
     """Merge ``o_parts [R, B, q_len, nh, 128]`` fp32 with ``lse_parts [R, B, q_len, nh]``.
 
-    Returns bf16 ``out [B, q_len, nh, 128]``, or ``(O fp32, LSE fp32)`` with ``return_lse``.
+    Returns bf16 ``out [B, q_len, nh, 128]`` (``torch.ops.solort_attn.lse_merge``), or
+    ``(O fp32, LSE fp32)`` with ``return_lse``.
     """
     _check_cuda("o_parts", o_parts, torch.float32)
-    _check_cuda("lse_parts", lse_parts, torch.float32)
-    if o_parts.dim() != 5 or o_parts.shape[-1] != HEAD_DIM:
+    if o_parts.dim() != 5:
         raise RuntimeError("o_parts must be [parts, batch, q_len, num_qo_heads, 128]")
     R, B, T, H, D = o_parts.shape
-    if tuple(lse_parts.shape) != (R, B, T, H):
-        raise RuntimeError("lse_parts must be [parts, batch, q_len, num_qo_heads]")
-    if not o_parts[0].is_contiguous() or not lse_parts[0].is_contiguous():
-        raise RuntimeError("each part of o_parts / lse_parts must be contiguous")
-    m = _lib.SolortMergeArgs()
-    m.o_parts, m.part_stride = o_parts.data_ptr(), o_parts.stride(0)
-    m.lse_parts, m.lse_part_stride = lse_parts.data_ptr(), lse_parts.stride(0)
-    m.num_parts, m.batch, m.q_len, m.num_qo_heads, m.head_dim = R, B, T, H, D
-    lse = None
     if return_lse:
         o32 = torch.empty(B, T, H, D, dtype=torch.float32, device=o_parts.device)
         lse = torch.empty(B, T, H, dtype=torch.float32, device=o_parts.device)
-        m.out_f32, m.lse_out = o32.data_ptr(), lse.data_ptr()
-        res = (o32, lse)
-    else:
-        if out is None:
-            out = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=o_parts.device)
-        m.out = out.data_ptr()
-        m.out_stride_batch, m.out_stride_token, m.out_stride_head = out.stride(0), out.stride(1), out.stride(2)
-        res = out
-    _lib.check(_lib.load().solort_attn_lse_merge(ctypes.byref(m), ctypes.c_void_p(_stream(o_parts.device))),
-               "solort_attn_lse_merge")
-    return res
-
+        _calls.lse_merge_into(o_parts, lse_parts, None, out_f32=o32, lse_out=lse)
+        return o32, lse
+    if out is None:
+        out = torch.empty(B, T, H, D, dtype=torch.bfloat16, device=o_parts.device)
+    _OPS.lse_merge(o_parts, lse_parts, out)
+    return out
 
 def decode_exchange_workspace_bytes(
     batch: int, q_len: int, num_qo_heads: int, num_kv_heads: int, max_kv_len: int,
@@ -651,7 +516,8 @@ def gqa_prefill(
     scale: float | None = None,
     out: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """Causal GQA prefill of one sequence on the tcgen05 tensor cores.
+    """Causal GQA prefill of one sequence on the tcgen05 tensor cores
+    (``torch.ops.solort_attn.gqa_prefill``).
 
     ``q [q_len, nh, 128]``, ``k, v [kv_len, nkv, 128]`` bf16 (token-major NHD views such as the
     reference's ``qkv.view(t, heads, hd)``; any token / head strides that are multiples of 8).
@@ -659,23 +525,19 @@ def gqa_prefill(
     of ``cuda_graph_executor.py:124-130`` and the HF bridge's bottom-right alignment
     (``transformers_flashinfer.py:182-193``). Returns ``out [q_len, nh, 128]`` bf16.
     """
-    for name, t in (("q", q), ("k", k), ("v", v)):
-        _check_cuda(name, t, torch.bfloat16)
-        if t.dim() != 3 or t.shape[-1] != HEAD_DIM or t.stride(-1) != 1:
-            raise RuntimeError(f"{name} must be [tokens, heads, 128] with a contiguous head dim")
-    if k.shape != v.shape or k.stride() != v.stride():
-        raise RuntimeError("k and v must have the same shape and strides")
-    T, H, D = q.shape
+    _check_cuda("q", q, torch.bfloat16)
     if out is None:
-        out = torch.empty(T, H, D, dtype=torch.bfloat16, device=q.device)
-    a = _lib.SolortPrefillArgs()
-    a.q, a.q_stride_token, a.q_stride_head = q.data_ptr(), q.stride(0), q.stride(1)
-    a.k, a.v = k.data_ptr(), v.data_ptr()
-    a.kv_stride_token, a.kv_stride_head = k.stride(0), k.stride(1)
-    a.out, a.out_stride_token, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
-    a.q_len, a.kv_len, a.num_qo_heads, a.num_kv_heads, a.head_dim = T, k.shape[0], H, k.shape[1], D
-    a.causal = 1 if causal else 0
-    a.scale = float(D ** -0.5 if scale is None else scale)
-    _lib.check(_lib.load().solort_attn_prefill(ctypes.byref(a), ctypes.c_void_p(_stream(q.device))),
-               "solort_attn_prefill")
+        out = torch.empty(q.shape, dtype=torch.bfloat16, device=q.device)
+    _OPS.gqa_prefill(q, k, v, out, bool(causal), scale)
     return out
+
+
+def kv_store(key: torch.Tensor, value: torch.Tensor, slots: torch.Tensor,
+             kv_pages: torch.Tensor) -> None:
+    """Write ``key / value [tokens, nkv, 128]`` (any token / head strides that are multiples of 8)
+    to physical slots ``slots`` (int64 on the device, ``page * P + row``) of one layer's paged
+    arena ``kv_pages [pages, 2, P, nkv, 128]`` (``torch.ops.solort_attn.kv_store``): the
+    slot-mapped store of ``PagedKVCache.store_layer_tokens`` (``kv_cache.py:191-235``) in one
+    launch instead of a Python loop over tokens."""
+    _OPS.kv_store(key, value, slots, kv_pages)
+

@@ -71,7 +71,8 @@ STRUCTS = [(_lib.SolortDecodeArgs, "SolortDecodeArgs"), (_lib.SolortMergeArgs, "
            (_lib.SolortPrologueArgs, "SolortPrologueArgs"),
            (_lib.SolortAddRmsNormArgs, "SolortAddRmsNormArgs"),
            (_lib.SolortSiluMulArgs, "SolortSiluMulArgs"),
-           (_lib.SolortGemvArgs, "SolortGemvArgs")]
+           (_lib.SolortGemvArgs, "SolortGemvArgs"),
+           (_lib.SolortKVStoreArgs, "SolortKVStoreArgs")]
 
 
 @pytest.mark.parametrize("cls,name", STRUCTS + ([(_lib.SolortPrefillArgs, "SolortPrefillArgs")]

@@ -39,7 +39,7 @@ def _static_case(seed, nh, nkv, L, q_len, cap=None):
 
 
 @pytest.mark.parametrize("nh,nkv", [(32, 8), (16, 8)])
-@pytest.mark.parametrize("L", [1, 7, 63, 64, 65, 200, 1024, 4097, 8192])
+@pytest.mark.parametrize("L", [1, 7, 63, 64, 65, 128, 200, 512, 1024, 2048, 4096, 4097, 8192])
 def test_decode_static_nhd(nh, nkv, L):
     ops = _ops()
     q, k, v = _static_case(L * 7 + nh, nh, nkv, L, 1)
@@ -277,6 +277,45 @@ def test_paged_decode_and_verify_shared_prefix():
     assert_close(out[0], ref_a, "paged verify seq A")
     assert_close(out[1, :1], ref_b, "paged decode seq B")
     assert (out[1, 1:].float() == 7.0).all(), "rows past q_lens must not be written"
+
+
+def test_paged_full_size_config4():
+    """BASELINE config 4 at full size: page size 16, context 16384, a pool of 2048 physical pages
+    handed out in a seeded random order, the first 4096 tokens (256 pages) shared by both block
+    tables (refcount 2). Sequence A verifies K = 4 drafts at positions 16384..16387 (each sees the
+    context plus the drafts before it); sequence B decodes one token at 16383. One call, ragged
+    q_lens, against the fp32 oracle on the device over the gathered dense K/V."""
+    ops = _ops()
+    P, ctx, shared, K, pool = 16, 16384, 256, 4, 2048
+    n_a, n_b = ctx + K, ctx
+    qa, ka, va = A.make_attention_inputs(41, 32, 8, 128, K, n_a, ctx)
+    qb, kb, vb = A.make_attention_inputs(42, 32, 8, 128, 1, n_b, ctx - 1)
+    kb[: shared * P] = ka[: shared * P]
+    vb[: shared * P] = va[: shared * P]
+    arena, tables = _paged_setup(43, [(n_a, ka, va), (n_b, kb, vb)], P, pool, shared_pages=shared)
+    assert len(set(tables[0]) | set(tables[1])) == len(tables[0]) + len(tables[1]) - shared
+    darena = arena.cuda()
+    dka, dva = OP.dense_from_block_table(darena, tables[0], n_a)
+    dkb, dvb = OP.dense_from_block_table(darena, tables[1], n_b)
+    assert torch.equal(dka.cpu(), ka) and torch.equal(dkb.cpu(), kb)
+    ref_a, _ = A.attention_fp32(qa.cuda(), dka, dva, 128**-0.5, ctx)
+    ref_b, _ = A.attention_fp32(qb.cuda(), dkb, dvb, 128**-0.5, ctx - 1)
+    bt = torch.zeros(2, max(len(t) for t in tables), dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, : len(t)] = torch.tensor(t, dtype=torch.int32)
+    q = torch.zeros(2, K, 32, 128, dtype=torch.bfloat16)
+    q[0] = qa
+    q[1, :1] = qb
+    qpos = torch.tensor([ctx, ctx - 1], dtype=torch.int64, device="cuda")
+    qlens = torch.tensor([K, 1], dtype=torch.int32, device="cuda")
+    out = torch.full((2, K, 32, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+    ops.gqa_decode_paged(q.cuda(), darena, bt.cuda(), qpos, max_kv_len=n_a, q_lens=qlens, out=out,
+                         stable_prefix=True)
+    torch.cuda.synchronize()
+    assert_close(out[0].cpu(), ref_a.cpu(), "config 4 verify, sequence A")
+    assert_close(out[1, :1].cpu(), ref_b.cpu(), "config 4 decode, sequence B")
+    assert (out[1, 1:].float() == 7.0).all(), "rows past q_lens must not be written"
+    assert ops.device_status() == 0
 
 
 @pytest.mark.parametrize("P", [8, 16, 64, 128])

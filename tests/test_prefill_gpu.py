@@ -21,7 +21,7 @@ def _close(got, ref, what):
     assert d.mean().item() <= MEAN_ABS, f"{what}: mean-abs {d.mean().item():.4g}"
 
 
-@pytest.mark.parametrize("T", [1, 17, 128, 200, 256, 511, 1024])
+@pytest.mark.parametrize("T", [1, 17, 128, 200, 256, 511, 512, 1024])
 @pytest.mark.parametrize("nh,nkv", [(32, 8), (16, 8)])
 def test_prefill_causal_square(T, nh, nkv):
     from solort_b200 import ops

@@ -3,11 +3,14 @@
 Some callers have no way to pass a workspace: a plugin host whose operator interface hands over
 only input and output buffers, or a host runtime that binds the C ABI without a CUDA allocator.
 `solort_attn_decode_static_scratch` serves them from a static 4 MiB device array inside the
-library. These tests call it through the C ABI twice in a row, on different shapes so the second
-call sees the first call's leftovers in the shared array, and compare each output with the regular
-`solort_attn_decode` (given a workspace) within the parity tolerance used everywhere else
-(max-abs 2e-2, mean-abs 2e-3). The file is collected last so a stop-at-first-failure run has run
-every other test before it; it passes alone in a fresh process too.
+library. These tests call it through the C ABI several times in a row and compare each output with
+the regular `solort_attn_decode` (given a workspace) and with the oracle, within the parity
+tolerance used everywhere else (max-abs 2e-2, mean-abs 2e-3): a full 8192-key decode; the same
+buffer, split count and row layout with the query at position 700, so 33 of the 37 splits hold no
+visible key and must overwrite the previous call's partials at the same offsets with empty ones;
+and a 5-token verify at 3000 keys, a different layout over the same array. The file is collected
+last so a stop-at-first-failure run has run every other test before it; it passes alone in a fresh
+process too.
 """
 
 from __future__ import annotations
@@ -41,16 +44,16 @@ def _close(got, ref, what):
     assert d.mean().item() <= MEAN_ABS, f"{what}: mean-abs {d.mean().item():.3g}"
 
 
-def test_static_scratch_matches_workspace_entry_point_on_two_calls():
+def test_static_scratch_matches_workspace_entry_point_on_calls_in_a_row():
     lib = _lib.load()
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    # decode at 8192 keys, then a 5-token verify at 3000: different split counts and row counts.
-    # An explicit split count keeps the split partials in scratch memory (without it, a single
-    # sequence's splits may merge inside a thread-block cluster and need no scratch at all).
-    for seed, L, q_len, splits in ((1, 8192, 1, 37), (2, 3000, 5, 12)):
-        q, k, v = A.make_attention_inputs(seed, 32, 8, 128, q_len, L, L - q_len)
+    # An explicit split count keeps the split partials in scratch memory: with one split a call
+    # needs no workspace at all. Calls: (seed, keys in the buffer, query rows, splits, q_pos).
+    for seed, L, q_len, splits, pos in ((1, 8192, 1, 37, 8191), (3, 8192, 1, 37, 700),
+                                        (2, 3000, 5, 12, 2995)):
+        q, k, v = A.make_attention_inputs(seed, 32, 8, 128, q_len, L, pos)
         dq, dk, dv = q[None].cuda(), k.cuda(), v.cuda()
-        qpos = torch.tensor([L - q_len], dtype=torch.int64, device="cuda")
+        qpos = torch.tensor([pos], dtype=torch.int64, device="cuda")
 
         out_ref = torch.empty_like(dq)
         a = _args(dq, dk, dv, qpos, out_ref, splits)
@@ -67,9 +70,9 @@ def test_static_scratch_matches_workspace_entry_point_on_two_calls():
         assert lib.solort_attn_decode_static_scratch(ctypes.byref(b), stream) == 0
         torch.cuda.synchronize()
 
-        _close(out_new, out_ref, f"static scratch vs workspace, L={L} q_len={q_len}")
-        ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, L - q_len)
-        _close(out_new[0].cpu(), ref, f"static scratch vs oracle, L={L} q_len={q_len}")
+        _close(out_new, out_ref, f"static scratch vs workspace, L={L} q_len={q_len} pos={pos}")
+        ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, pos)
+        _close(out_new[0].cpu(), ref, f"static scratch vs oracle, L={L} q_len={q_len} pos={pos}")
     assert ops.device_status() == 0
 
 
