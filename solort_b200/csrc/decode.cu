@@ -1,4 +1,7 @@
 // Split-KV GQA decode / verify for sm_100a, static or paged KV, with the log-sum-exp merge.
+// Two split kernels share the plan, the partial layout and the merge: decode_kernel (mma.sync,
+// below) for short splits, where a call is latency-bound, and decode_tc_kernel (tcgen05 / TMEM,
+// further down) for long splits of at most four query rows, where the tile stream dominates.
 //
 // decode_kernel: one CTA per (key split, KV head, sequence). Its KV rows stream through a 7-stage
 // ring of 16 KB shared-memory stages (32 tokens of K and V, two 64-dim halves each) filled by TMA
@@ -30,6 +33,7 @@
 
 #include "common.cuh"
 #include "host_util.h"
+#include "tcgen05.cuh"
 
 namespace solort {
 
@@ -583,6 +587,542 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
   }
 }
 
+// ------------------------------------------------------------------------------------------
+// decode_tc_kernel: the same split-KV decode on the 5th-generation tensor cores. The plan picks it
+// for splits of at least kMinChunk keys with at most four query rows per KV head (RB, the
+// compile-time row bound, is 4); there it streams a split's tiles faster than decode_kernel
+// (131072 keys: 86.6 vs 89 us per layer). On short splits it loses: each 64-key tile costs ~1800
+// cycles of hand-offs (QK commit -> TMEM load -> cross-warp row max -> P store -> PV issue),
+// against decode_kernel's per-warp tile loop that needs no exchange until the end.
+//
+// The query rows are the narrow side, so both products are transposed: S^T = K Q^T with the keys
+// as M (tcgen05.mma M = 64, N = 16 query rows, K = 128 dims) and O^T = V^T P^T with the head dims
+// as M (M = 128, N = 16, K = 64 keys, V^T read as an MN-major operand straight from the TMA
+// tiles). The tensor core reads K and V from shared memory itself -- no ldmatrix pass through the
+// register file -- and its throughput makes the rows padded up to 16 cost little. S^T of a 64-key
+// tile lands in TMEM with key m in lane (m % 16) + 32 (m / 16) (the M = 64 layout): warp w's
+// lanes 0-15 hold keys 16w..16w+15, one column per query row. Four softmax warps read it, take
+// the tile's row maxima (16-lane shuffles, then the four warps through shared memory), keep one
+// running maximum per row with lazy rescaling (O in TMEM is rescaled only when a row's maximum
+// grows by more than 2^8), and write P^T as bf16 for the PV MMA. One thread issues the MMAs, one
+// the TMA copies. 64-key tiles cycle through a 3-tile ring (three 8 KB slots in each of four 24 KB
+// regions: K dims 0-63, K dims 64-127, V dims 0-63, V dims 64-127); tiles past the ring are
+// prefetched into L2 so their refill is an L2 read. At the end each thread owns one head dim of
+// every row (O^T lane = dim), so the epilogue is one TMEM load, the row sums, and coalesced
+// stores of the partial (O, LSE) or the final bf16 rows.
+// ------------------------------------------------------------------------------------------
+namespace tc {
+constexpr int kTileKeys = 64;
+constexpr int kSlots = 3;
+constexpr int kRegionRows = kTileKeys * kSlots;  // 192
+constexpr int kRegionBytes = kRegionRows * 128;  // 24 KB
+constexpr int kSlotBytes = kTileKeys * 128;      // 8 KB
+constexpr int kN = 16;                           // query rows per MMA
+constexpr int kOffK0 = 0;
+constexpr int kOffK1 = kRegionBytes;
+constexpr int kOffV0 = 2 * kRegionBytes;
+constexpr int kOffV1 = 3 * kRegionBytes;
+constexpr int kQHalf = kN * 128;                  // one 64-dim half of the query rows: 2 KB
+constexpr int kOffQ = 4 * kRegionBytes;           // 96 KB
+constexpr int kPBytes = kN * 128;                 // P^T of one tile: 2 KB
+constexpr int kOffP = kOffQ + 2 * kQHalf;         // two P buffers
+constexpr int kOffHdr = kOffP + 2 * kPBytes;      // 104 KB
+enum {
+  kBarFull = 0,                        // +slot: TMA bytes of a tile landed
+  kBarSFull = kBarFull + kSlots,       // +S buffer: QK committed
+  kBarSFree = kBarSFull + 2,           // +S buffer: 128 softmax threads read it
+  kBarPFull = kBarSFree + 2,           // +P buffer: 128 threads wrote P (and rescaled O)
+  kBarPFree = kBarPFull + 2,           // +P buffer: PV committed
+  kBarSlotFree = kBarPFree + 2,        // +slot: PV of the slot's tile committed
+  kBarXMax = kBarSlotFree + kSlots,    // +tile parity: row maxima exchanged (128 arrivals)
+  kBarXSum = kBarXMax + 2,             // row sums exchanged (128 arrivals)
+  kBarQ = kBarXSum + 1,                // query rows staged (128 arrivals)
+  kBarOFinal = kBarQ + 1,              // every MMA done
+  kNumBars = kBarOFinal + 1
+};
+constexpr int kHdrInts = 8;  // [0] abort, [1] TMEM base, [2..4] tile last issued per slot
+constexpr int kOffRedMax = kOffHdr + kNumBars * 8 + kHdrInts * 4;  // [2][4][kN] fp32
+constexpr int kOffRedL = kOffRedMax + 2 * 4 * kN * 4;              // [4][kN] fp32
+constexpr int kOffBt = kOffRedL + 4 * kN * 4;                      // block-table slice
+constexpr int kThreads = 192;  // warps 0-3 softmax + epilogue, 4 MMA issue, 5 TMA producer
+constexpr int kSoftmaxThreads = 128;
+constexpr uint32_t kTmemCols = 64;  // S^T x 2 (16 columns each), O^T (16)
+// Lazy rescaling: O^T in TMEM is rescaled only when a row's tile maximum exceeds the reference
+// it was accumulated against by more than 2^64 (log2 domain). P <= 2^64 stays finite in bf16, and
+// O and the row sums stay below 2^64 * 2^14 keys * |v| in fp32, far from overflow; scores of a real
+// model rarely move the maximum that much, so the pipeline-draining rescale almost never runs.
+constexpr float kRescaleLog2 = 64.f;
+constexpr int kMinChunk = 2048;  // keys per split from which the plan picks this kernel
+constexpr uint32_t kIdescQK = umma::idesc_bf16(64, kN, false, false);
+constexpr uint32_t kIdescPV = umma::idesc_bf16(128, kN, true, false);
+static_assert(kOffBt % 4 == 0, "block-table slice alignment");
+}  // namespace tc
+
+// Bounded mbarrier wait that also gives up once another role has aborted.
+// Waiting threads suspend in hardware (up to 20 us per try, resuming when the phase completes), so
+// the MMA-issue and TMA threads do not take issue slots from the softmax warps while they wait.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_suspend(addr, parity, 20000u)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      atomicOr(&g_decode_status, kDevErrBarrierTimeout);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+// One element of a finished row: bf16 output, or fp32 output + LSE (partial-output mode).
+__device__ __forceinline__ void write_final1(const Params& p, int R, int d, float v, float lse) {
+  if (p.out_f32) {
+    p.out_f32[static_cast<int64_t>(R) * kHD + d] = v;
+    if (d == 0) p.lse_out[R] = lse;
+  } else {
+    const int h = R % p.nh, t = (R / p.nh) % p.q_len, b = R / (p.nh * p.q_len);
+    p.out[b * p.o_sb + t * p.o_st + h * p.o_sh + d] = __float2bfloat16_rn(v);
+  }
+}
+
+template <bool PAGED, int RB>
+__global__ void __launch_bounds__(tc::kThreads, 2)
+    decode_tc_kernel(const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const Params p) {
+  using namespace tc;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = smem_raw;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + kOffHdr);
+  int* hdr = reinterpret_cast<int*>(bars + kNumBars);
+  volatile int* abort_flag = hdr;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(hdr + 1);
+  int* last_fill = hdr + 2;
+  float* red_max = reinterpret_cast<float*>(sm + kOffRedMax);
+  float* red_l = reinterpret_cast<float*>(sm + kOffRedL);
+  int* bt_s = reinterpret_cast<int*>(sm + kOffBt);
+  const uint32_t sbase = smem_u32(sm);
+
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y;
+  const int b = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int rows_total = p.batch * p.q_len * p.nh;
+  const bool single = p.num_splits == 1 && !p.force_partial;
+
+  pdl_launch_dependents();
+  if (sbase & 1023u) {
+    if (tid == 0) atomicOr(&g_decode_status, kDevErrSmemAlign);
+    return;
+  }
+  if (tid == 0) {
+    prefetch_tensormap(&tmK);
+    prefetch_tensormap(&tmV);
+    for (int i = 0; i < kNumBars; ++i) {
+      const bool many = (i >= kBarSFree && i < kBarSFree + 2) || (i >= kBarPFull && i < kBarPFull + 2) ||
+                        (i >= kBarXMax && i < kBarXSum + 1) || i == kBarQ;
+      mbar_init(&bars[i], many ? kSoftmaxThreads : 1);
+    }
+    hdr[0] = 0;
+    for (int s = 0; s < kSlots; ++s) last_fill[s] = -1;
+    fence_mbarrier_init();
+  }
+  const bool early = p.stable_prefix != 0;
+  if (warp < 4) {  // warm L2 with the query rows (a hint: they are read after the wait)
+    for (int idx = tid; idx < p.q_len * p.group * 2; idx += kSoftmaxThreads) {
+      const int r = idx >> 1;
+      const bf16* src = p.q + b * p.q_sb + (r / p.group) * p.q_st +
+                        (kvh * p.group + r % p.group) * p.q_sh + (idx & 1) * 64;
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(src));
+    }
+  }
+  if (!early) pdl_wait();
+
+  const long long qpos = p.q_pos[b];
+  const int qlen_b = p.q_lens ? min(p.q_lens[b], p.q_len) : p.q_len;
+  const int rows_b = qlen_b * p.group;
+  long long kv_end_ll = qpos + qlen_b - p.kv_pos_offset;
+  kv_end_ll = kv_end_ll < 0 ? 0 : kv_end_ll;
+  kv_end_ll = kv_end_ll > p.kv_limit ? p.kv_limit : kv_end_ll;
+  const int kv_end = static_cast<int>(kv_end_ll);
+  const int t_begin = split * p.chunk;
+  const int t_end = min(t_begin + p.chunk, kv_end);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + kTileKeys - 1) / kTileKeys : 0;
+  auto out_row = [&](int r) {
+    return (b * p.q_len + r / p.group) * p.nh + kvh * p.group + r % p.group;
+  };
+
+  if (ntiles == 0) {
+    // Nothing visible in this split: an empty partial (O = 0, LSE = -inf), or zero final rows.
+    if (early) pdl_wait();
+    for (int idx = tid; idx < rows_b * kHD; idx += kThreads) {
+      const int r = idx / kHD, d = idx % kHD;
+      if (single)
+        write_final1(p, out_row(r), d, 0.f, -INFINITY);
+      else {
+        p.part_o[(static_cast<int64_t>(split) * rows_total + out_row(r)) * kHD + d] = 0.f;
+        if (d == 0) p.part_lse[static_cast<int64_t>(split) * rows_total + out_row(r)] = -INFINITY;
+      }
+    }
+    return;
+  }
+
+  int lp0 = 0;
+  if (PAGED) {
+    lp0 = t_begin >> p.page_shift;
+    const int lp1 = (t_end - 1) >> p.page_shift;
+    for (int i = tid; i <= lp1 - lp0; i += kThreads)
+      bt_s[i] = p.block_table[b * p.bt_stride + lp0 + i];
+  }
+  if (warp == 0) umma::alloc(tmem_slot, kTmemCols);
+  umma::fence_before();
+  __syncthreads();
+  umma::fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tO = tmem + 2 * kN;
+
+  // TMA coordinates of the box of `tok` rows (map coordinate order as the tensor maps define).
+  auto coords = [&](int tok, int& c1, int& c2, int& c3) {
+    if (!PAGED) {
+      c1 = p.tok_coord == 1 ? tok : kvh;
+      c2 = p.tok_coord == 1 ? kvh : tok;
+      c3 = 0;
+    } else {
+      const int row = tok & (p.page_size - 1);
+      c1 = p.tok_coord == 1 ? row : kvh;
+      c2 = p.tok_coord == 1 ? kvh : row;
+      c3 = bt_s[(tok >> p.page_shift) - lp0];
+    }
+  };
+  // Fill slot s with the boxes of tile `it` that hold keys of this split; rows of the slot past
+  // the split end keep stale contents (masked for K, zeroed for V before the PV MMA).
+  auto issue = [&](int it, int s) {
+    const int t0 = t_begin + it * kTileKeys;
+    const int br = p.box_rows;
+    const int nbox = (min(kTileKeys, t_end - t0) + br - 1) / br;
+    last_fill[s] = it;
+    mbar_arrive_expect_tx(&bars[kBarFull + s], static_cast<uint32_t>(nbox * br * 128 * 4));
+    for (int j = 0; j < nbox; ++j) {
+      int c1, c2, c3;
+      coords(t0 + j * br, c1, c2, c3);
+      const int off = s * kSlotBytes + j * br * 128;
+      tma_load_4d(sm + kOffK0 + off, &tmK, &bars[kBarFull + s], 0, c1, c2, c3);
+      tma_load_4d(sm + kOffK1 + off, &tmK, &bars[kBarFull + s], 64, c1, c2, c3);
+      tma_load_4d(sm + kOffV0 + off, &tmV, &bars[kBarFull + s], 0, c1, c2, c3);
+      tma_load_4d(sm + kOffV1 + off, &tmV, &bars[kBarFull + s], 64, c1, c2, c3);
+    }
+  };
+  auto prefetch = [&](int it) {
+    const int t0 = t_begin + it * kTileKeys;
+    const int br = p.box_rows;
+    const int nbox = (min(kTileKeys, t_end - t0) + br - 1) / br;
+    for (int j = 0; j < nbox; ++j) {
+      int c1, c2, c3;
+      coords(t0 + j * br, c1, c2, c3);
+      tma_prefetch_l2_4d(&tmK, 0, c1, c2, c3);
+      tma_prefetch_l2_4d(&tmK, 64, c1, c2, c3);
+      tma_prefetch_l2_4d(&tmV, 0, c1, c2, c3);
+      tma_prefetch_l2_4d(&tmV, 64, c1, c2, c3);
+    }
+  };
+
+  if (warp == 5) {
+    // ---- TMA producer ----
+    if (lane == 0) {
+      const int n0 = min(ntiles, kSlots);
+      const int pre_end = min(ntiles, 2 * kSlots);
+      int i = 0;
+      if (early) {
+        // Tiles whose keys all lie below q_pos were written before the previous kernel.
+        const long long stable_end = qpos - p.kv_pos_offset;
+        while (i < n0 && min(t_begin + (i + 1) * kTileKeys, t_end) <= stable_end) {
+          issue(i, i);
+          ++i;
+        }
+        for (int it = kSlots; it < pre_end; ++it)
+          if (min(t_begin + (it + 1) * kTileKeys, t_end) <= stable_end) prefetch(it);
+        pdl_wait();
+      }
+      for (; i < n0; ++i) issue(i, i);
+      if (!early)
+        for (int it = kSlots; it < pre_end; ++it) prefetch(it);
+      for (int t = kSlots; t < ntiles; ++t) {
+        const int s = t % kSlots;
+        if (!tc_wait(&bars[kBarSlotFree + s], ((t - kSlots) / kSlots) & 1, abort_flag)) break;
+        issue(t, s);
+        if (t + kSlots < ntiles) prefetch(t + kSlots);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 4) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      bool ok = tc_wait(&bars[kBarQ], 0, abort_flag);
+      auto pv = [&](int u) -> bool {
+        const int bu = u & 1, su = u % kSlots;
+        if (!tc_wait(&bars[kBarPFull + bu], (u >> 1) & 1, abort_flag)) return false;
+        umma::fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kTileKeys / 16; ++kk) {
+          // V^T: MN-major (dims contiguous), 16 keys = two 8-row groups; the 64-dim halves are
+          // one region apart. P^T: K-major, 16 keys = 32 bytes of each 128-byte row.
+          const uint64_t da = umma::smem_desc(sbase + kOffV0 + su * kSlotBytes + kk * 2048,
+                                              kRegionBytes, 1024);
+          const uint64_t db = umma::smem_desc(sbase + kOffP + bu * kPBytes + kk * 32, 16, 1024);
+          umma::mma_ss(tO, da, db, kIdescPV, (u > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma::commit(&bars[kBarSlotFree + su]);
+        umma::commit(&bars[kBarPFree + bu]);
+        return true;
+      };
+      for (int t = 0; ok && t < ntiles; ++t) {
+        const int s = t % kSlots, bb = t & 1;
+        if (!tc_wait(&bars[kBarFull + s], (t / kSlots) & 1, abort_flag) ||
+            (t >= 2 && !tc_wait(&bars[kBarSFree + bb], ((t - 2) >> 1) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        umma::fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kHD / 16; ++kk) {
+          const uint32_t ka = (kk < 4 ? kOffK0 : kOffK1) + s * kSlotBytes + (kk & 3) * 32;
+          const uint32_t qb = kOffQ + (kk >> 2) * kQHalf + (kk & 3) * 32;
+          umma::mma_ss(tmem + bb * kN, umma::smem_desc(sbase + ka, 16, 1024),
+                       umma::smem_desc(sbase + qb, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+        }
+        umma::commit(&bars[kBarSFull + bb]);
+        if (t >= 1 && !pv(t - 1)) ok = false;
+      }
+      if (ok) pv(ntiles - 1);
+      umma::commit(&bars[kBarOFinal]);  // arrives once every MMA issued above has completed
+    }
+    __syncwarp();
+  } else {
+    // ---- softmax + epilogue (warps 0-3) ----
+    // Every per-row sequence below is written step-major (all rows' shuffles of one step, all
+    // loads before their uses) so that the rows' latency chains overlap; RB bounds the live rows
+    // at compile time.
+    if (early) pdl_wait();
+    // Query rows into the B operand of S^T = K Q^T: K-major, 128-byte swizzle, two 64-dim halves;
+    // rows past q_len * group are zero.
+    const int rows_alloc = p.q_len * p.group;
+    for (int idx = tid; idx < kN * 16; idx += kSoftmaxThreads) {
+      const int r = idx >> 4, c = idx & 15;
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (r < rows_alloc) {
+        const bf16* src = p.q + b * p.q_sb + (r / p.group) * p.q_st +
+                          (kvh * p.group + r % p.group) * p.q_sh + c * 8;
+        if (p.q_vec16) {
+          v = *reinterpret_cast<const uint4*>(src);
+        } else {
+          const uint32_t* s32 = reinterpret_cast<const uint32_t*>(src);
+          v = make_uint4(s32[0], s32[1], s32[2], s32[3]);
+        }
+      }
+      *reinterpret_cast<uint4*>(sm + kOffQ + (c >> 3) * kQHalf + (r >> 3) * 1024 + (r & 7) * 128 +
+                                (((c & 7) ^ (r & 7)) << 4)) = v;
+    }
+    fence_proxy_async_shared();
+    mbar_arrive(&bars[kBarQ]);
+
+    int lim[RB];  // last visible local key of each row (-1: none)
+    float m_run[RB], l_part[RB];
+#pragma unroll
+    for (int r = 0; r < RB; ++r) {
+      long long last = qpos + r / p.group - p.kv_pos_offset;
+      last = last < t_end - 1 ? last : t_end - 1;
+      lim[r] = r < rows_b ? static_cast<int>(last < -1 ? -1 : last) : -1;
+      m_run[r] = -INFINITY;
+      l_part[r] = 0.f;
+    }
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const int kl = warp * 16 + lane;  // this lane's key within a tile (lanes 0-15)
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      const int bb = t & 1, s = t % kSlots;
+      if (!__all_sync(0xffffffffu, tc_wait(&bars[kBarSFull + bb], (t >> 1) & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      umma::fence_after();
+      float sv[16];
+      if (RB <= 4)
+        umma::ld4(tmem + bb * kN + lane_off, sv);
+      else
+        umma::ld16(tmem + bb * kN + lane_off, sv);
+      umma::wait_ld();
+      umma::fence_before();
+      mbar_arrive(&bars[kBarSFree + bb]);
+      const int key = t_begin + t * kTileKeys + kl;
+      float v[RB], m[RB];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        v[r] = (lane < 16 && key <= lim[r]) ? sv[r] * p.scale_log2 : -INFINITY;
+        m[r] = v[r];
+      }
+      // tile row maxima: 16 lanes, then the four warps through shared memory
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        float x[RB];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) x[r] = __shfl_xor_sync(0xffffffffu, m[r], o);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) m[r] = fmaxf(m[r], x[r]);
+      }
+      float* rm = red_max + bb * 4 * kN;
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r) rm[warp * kN + r] = m[r];
+      }
+      mbar_arrive(&bars[kBarXMax + bb]);
+      if (!__all_sync(0xffffffffu, tc_wait(&bars[kBarXMax + bb], (t >> 1) & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      float w4[4][RB];
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+#pragma unroll
+        for (int r = 0; r < RB; ++r) w4[w][r] = rm[w * kN + r];
+      bool grow = false;
+      float alpha[RB];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        const float mt = fmaxf(fmaxf(w4[0][r], w4[1][r]), fmaxf(w4[2][r], w4[3][r]));
+        const float mo = m_run[r];
+        alpha[r] = 1.f;
+        if (mt > -INFINITY && (mo == -INFINITY || mt > mo + kRescaleLog2)) {
+          m_run[r] = mt;
+          if (mo != -INFINITY) {
+            alpha[r] = exp2f(mo - mt);
+            grow = true;
+          }
+        }
+      }
+      if (grow) {
+        // O^T holds the PV of tiles < t against the old maxima: wait for PV_{t-1}, rescale.
+        if (!__all_sync(0xffffffffu, tc_wait(&bars[kBarSlotFree + (t - 1) % kSlots],
+                                             ((t - 1) / kSlots) & 1, abort_flag))) {
+          ok = false;
+          break;
+        }
+        umma::fence_after();
+        float ov[kN];
+        umma::ld16(tO + lane_off, ov);
+        umma::wait_ld();
+#pragma unroll
+        for (int r = 0; r < RB; ++r) ov[r] *= alpha[r];
+        umma::st16(tO + lane_off, ov);
+        umma::wait_st();
+#pragma unroll
+        for (int r = 0; r < RB; ++r) l_part[r] *= alpha[r];
+      }
+      float e[RB];
+#pragma unroll
+      for (int r = 0; r < RB; ++r) {
+        e[r] = v[r] == -INFINITY ? 0.f : exp2f(v[r] - m_run[r]);
+        l_part[r] += e[r];
+      }
+      // P buffer bb was last read by PV_{t-2}.
+      if (t >= 2 && !__all_sync(0xffffffffu,
+                                tc_wait(&bars[kBarPFree + bb], ((t - 2) >> 1) & 1, abort_flag))) {
+        ok = false;
+        break;
+      }
+      // P^T rows past RB feed O^T columns nobody reads and stay unwritten.
+      uint8_t* pbuf = sm + kOffP + bb * kPBytes;
+      if (lane < 16) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r)
+          *reinterpret_cast<bf16*>(pbuf + (r >> 3) * 1024 + (r & 7) * 128 +
+                                   (((kl >> 3) ^ (r & 7)) << 4) + (kl & 7) * 2) =
+              __float2bfloat16_rn(e[r]);
+      }
+      // Rows of the slot past the split end hold stale data: P is 0 there, but 0 * NaN is not,
+      // so zero those V rows before the PV MMA reads them.
+      const int valid = t_end - (t_begin + t * kTileKeys);
+      if (valid < kTileKeys) {
+        for (int idx = tid; idx < (kTileKeys - valid) * 16; idx += kSoftmaxThreads) {
+          const int row = valid + (idx >> 4), c = idx & 15;
+          uint8_t* vb = sm + ((c >> 3) ? kOffV1 : kOffV0) + s * kSlotBytes;
+          *reinterpret_cast<uint4*>(vb + row * 128 + (((c & 7) ^ (row & 7)) << 4)) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_shared();
+      umma::fence_before();
+      mbar_arrive(&bars[kBarPFull + bb]);
+    }
+
+    if (ok && !__all_sync(0xffffffffu, tc_wait(&bars[kBarOFinal], 0, abort_flag))) ok = false;
+    if (ok) {
+      umma::fence_after();
+      float ov[16];
+      if (RB <= 4)
+        umma::ld4(tO + lane_off, ov);
+      else
+        umma::ld16(tO + lane_off, ov);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        float x[RB];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) x[r] = __shfl_xor_sync(0xffffffffu, l_part[r], o);
+#pragma unroll
+        for (int r = 0; r < RB; ++r) l_part[r] += x[r];
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < RB; ++r) red_l[warp * kN + r] = l_part[r];
+      }
+      umma::wait_ld();
+      mbar_arrive(&bars[kBarXSum]);
+      if (__all_sync(0xffffffffu, tc_wait(&bars[kBarXSum], 0, abort_flag))) {
+        float w4[4][RB];
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+#pragma unroll
+          for (int r = 0; r < RB; ++r) w4[w][r] = red_l[w * kN + r];
+        const int d = warp * 32 + lane;  // O^T lane = head dim
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          if (r < rows_b) {
+            const float L = (w4[0][r] + w4[1][r]) + (w4[2][r] + w4[3][r]);
+            const float val = L > 0.f ? ov[r] * __frcp_rn(L) : 0.f;
+            const float lse = L > 0.f ? (m_run[r] + __log2f(L)) * kLn2 : -INFINITY;
+            const int R = out_row(r);
+            if (single) {
+              write_final1(p, R, d, val, lse);
+            } else {
+              p.part_o[(static_cast<int64_t>(split) * rows_total + R) * kHD + d] = val;
+              if (d == 0) p.part_lse[static_cast<int64_t>(split) * rows_total + R] = lse;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  // ---- teardown: nothing may be in flight when the CTA releases TMEM and shared memory ----
+  umma::fence_before();
+  __syncthreads();
+  if (*abort_flag && tid == 0) {
+    const unsigned long long t0 = globaltimer_ns();
+    auto drain = [&](uint64_t* bar, uint32_t parity) {
+      while (!mbar_try_wait(smem_u32(bar), parity) && globaltimer_ns() - t0 < kWaitLimitNs) {
+      }
+    };
+    for (int s = 0; s < kSlots; ++s)
+      if (last_fill[s] >= 0) drain(&bars[kBarFull + s], (last_fill[s] / kSlots) & 1);
+    drain(&bars[kBarOFinal], 0);
+  }
+  __syncthreads();
+  umma::fence_after();
+  if (warp == 0) umma::dealloc(tmem, kTmemCols);
+}
+
 struct MergeParams {
   const float* o_parts;
   int64_t part_stride;
@@ -708,6 +1248,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32) merge_kernel(const MergePara
 
 struct Plan {
   int mt = 1;
+  bool tc = false;  // up to 16 query rows per KV head: the tcgen05 kernel
   bool paged = false;
   int kv_limit = 0;
   int chunk = 0;
@@ -734,6 +1275,7 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl, bool force_partial = false) {
   const int rows = a->q_len * group;
   if (rows > 32) return SOLORT_ERR_UNSUPPORTED;
   pl->mt = rows <= 16 ? 1 : 2;
+  pl->tc = false;  // decided below, once the split length is known
   pl->paged = a->block_table != nullptr;
   if (a->max_kv_len <= 0) return SOLORT_ERR_INVALID_ARGUMENT;
   if (pl->paged) {
@@ -769,8 +1311,17 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl, bool force_partial = false) {
     pl->part_lse_bytes = align_up(static_cast<size_t>(pl->splits) * pl->rows_total * 4, 256);
   }
   pl->ws_bytes = pl->part_o_bytes + pl->part_lse_bytes;
-  // The block-table slice of a split sits after the ring; a long one costs the ring a stage.
   const int bt_ints = pl->paged ? (pl->chunk / a->page_size + 2) : 0;
+  // Long splits of at most four query rows run on the tcgen05 kernel, whose tile pipeline streams
+  // faster; short splits are latency-bound, where the mma.sync kernel's per-warp tile loop (no
+  // cross-warp exchange per tile) finishes first.
+  pl->tc = rows <= 4 && pl->chunk >= tc::kMinChunk;
+  if (pl->tc) {
+    pl->smem_bytes = static_cast<size_t>(tc::kOffBt) + bt_ints * 4;
+    if (pl->smem_bytes > static_cast<size_t>(kSmemPerCta)) return SOLORT_ERR_UNSUPPORTED;
+    return SOLORT_OK;
+  }
+  // The block-table slice of a split sits after the ring; a long one costs the ring a stage.
   const int spare = kSmemPerCta - kMaxStages * kStageBytes - kHdrBytes;
   pl->stages = bt_ints * 4 <= spare ? kMaxStages : kMaxStages - 1;
   pl->smem_bytes = static_cast<size_t>(pl->stages) * kStageBytes + kHdrBytes + bt_ints * 4;
@@ -812,6 +1363,29 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& pr
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(grid, dim3(Shape<MT>::kThreads), smem, stream, attr);
   if (cudaLaunchKernelEx(&cfg, decode_kernel<MT, PAGED>, tk, tv, prm) != cudaSuccess)
+    return SOLORT_ERR_CUDA;
+  return launch_status();
+}
+
+template <bool PAGED, int RB>
+int launch_decode_tc(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, dim3 grid,
+                     size_t smem, cudaStream_t stream) {
+  static std::atomic<unsigned> configured{0};  // one bit per device ordinal < 32
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return SOLORT_ERR_CUDA;
+  if (smem > static_cast<size_t>(kSmemPerCta)) return SOLORT_ERR_UNSUPPORTED;
+  if (dev >= 32 || !(configured.load(std::memory_order_acquire) & (1u << dev))) {
+    if (cudaFuncSetAttribute(decode_tc_kernel<PAGED, RB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemPerCta) != cudaSuccess ||
+        cudaFuncSetAttribute(decode_tc_kernel<PAGED, RB>,
+                             cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared) != cudaSuccess)
+      return SOLORT_ERR_CUDA;
+    if (dev < 32) configured.fetch_or(1u << dev, std::memory_order_release);
+  }
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pdl_config(grid, dim3(tc::kThreads), smem, stream, attr);
+  if (cudaLaunchKernelEx(&cfg, decode_tc_kernel<PAGED, RB>, tk, tv, prm) != cudaSuccess)
     return SOLORT_ERR_CUDA;
   return launch_status();
 }
@@ -1019,7 +1593,10 @@ int decode_impl(const SolortDecodeArgs* a, const SolortExchangeArgs* x, void* st
 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   dim3 grid(pl.splits, a->num_kv_heads, a->batch);
-  if (pl.mt == 1) {
+  if (pl.tc) {
+    rc = pl.paged ? launch_decode_tc<true, 4>(tk, tv, prm, grid, pl.smem_bytes, stream)
+                  : launch_decode_tc<false, 4>(tk, tv, prm, grid, pl.smem_bytes, stream);
+  } else if (pl.mt == 1) {
     rc = pl.paged ? launch_decode<1, true>(tk, tv, prm, grid, pl.smem_bytes, stream)
                   : launch_decode<1, false>(tk, tv, prm, grid, pl.smem_bytes, stream);
   } else {
