@@ -8,8 +8,11 @@ L2). Inputs are seeded synthetic tensors with the reference's pipeline: N(0,1) -
 (eps 1e-6) -> RoPE (theta 1e6). The 36 calls are captured in one CUDA graph and replayed.
 
 N > 1 (torchrun): the sequence is sharded, context 8192 * N with 8192 keys per rank (weak
-scaling); per layer each rank computes a partial (O, LSE) of its shard, the partials are
-all-gathered with NCCL over NVLink and merged with the LSE-merge kernel on every rank.
+scaling, the headline); per layer each rank computes a partial (O, LSE) of its shard and the
+partials meet over NVLink (peer stores, or NCCL all-gather) and are merged on every rank. The
+``config5`` section measures BASELINE config 5 as specified at every N: a fixed 131072-key
+context, 131072 / N keys per rank (strong scaling), both exchanges, with the single-GPU time of
+the whole context measured in the same run.
 
 Prints ONE JSON line (rank 0). ``value`` = KV bytes read by all ranks per second (GB/s).
 ``--impl reference`` times the reference's CPU attention path (the grouped decode of
@@ -59,6 +62,8 @@ def parse_args():
     ap.add_argument("--no-stable-prefix", action="store_true",
                     help="decode calls without SOLORT_DECODE_STABLE_PREFIX (keys requested only "
                          "after the previous kernel finished)")
+    ap.add_argument("--no-config5", action="store_true",
+                    help="skip the 131072-key strong-scaling section (BASELINE config 5)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the paged / long-context / tok/s sections of the default line")
     return ap.parse_args()
@@ -138,23 +143,23 @@ def _rope(x, pos, dtype):
     return x * cos + torch.cat([-x[..., h:], x[..., :h]], -1) * sin
 
 
-def make_inputs(ctx: int, rank: int, world: int, device, seed: int = 2024):
-    """KV [36, 2, 8, ctx, 128] for keys [rank*ctx, (rank+1)*ctx) of a ctx*world context, and the
-    36 layers' query [36, 1, 1, 32, 128] at position ctx*world - 1 (same on every rank)."""
+def make_inputs(ctx: int, rank: int, world: int, device, seed: int = 2024, layers: int = LAYERS):
+    """KV [layers, 2, 8, ctx, 128] for keys [rank*ctx, (rank+1)*ctx) of a ctx*world context, and
+    the layers' query [layers, 1, 1, 32, 128] at position ctx*world - 1 (same on every rank)."""
     import torch
 
     bf = torch.bfloat16
-    kv = torch.empty(LAYERS, 2, NKV, ctx, HD, dtype=bf, device=device)
+    kv = torch.empty(layers, 2, NKV, ctx, HD, dtype=bf, device=device)
     pos = torch.arange(rank * ctx, (rank + 1) * ctx, device=device)
     g = torch.Generator(device=device)
-    for li in range(LAYERS):
+    for li in range(layers):
         g.manual_seed(seed * 1000 + li * 16 + rank)
         k = torch.randn(ctx, NKV, HD, generator=g, device=device).to(bf)
         v = torch.randn(ctx, NKV, HD, generator=g, device=device).to(bf)
         kv[li, 0] = _rope(_rmsnorm(k), pos, bf).transpose(0, 1)
         kv[li, 1] = v.transpose(0, 1)
     g.manual_seed(seed)
-    q = torch.randn(LAYERS, 1, 1, NH, HD, generator=g, device=device).to(bf)
+    q = torch.randn(layers, 1, 1, NH, HD, generator=g, device=device).to(bf)
     qpos = torch.full((1,), ctx * world - 1, dtype=torch.int64, device=device)
     q = _rope(_rmsnorm(q), qpos.repeat(1), bf)
     return kv, q, qpos
@@ -227,6 +232,109 @@ def run_reference_arm(args) -> None:
 # ------------------------------------------------------------------------------------------
 # GPU arm
 # ------------------------------------------------------------------------------------------
+
+CONFIG5_KEYS, CONFIG5_LAYERS = 131072, 8
+
+
+def config5_bench(dev, rank: int, world: int, steps: int) -> dict:
+    """BASELINE config 5 as specified: a fixed 131072-key context sharded over the N ranks
+    (131072 / N contiguous keys each; strong scaling), CONFIG5_LAYERS layers per step, every
+    exchange the library offers for N > 1. Reports the per-layer time (max over ranks), the KV
+    bytes of all ranks per second and per rank, and the strong-scaling efficiency T1 / (N * TN)
+    against the single-GPU decode of the whole context timed on rank 0 in the same run."""
+    import torch
+    import torch.distributed as dist
+
+    from solort_b200 import ops
+
+    shard = CONFIG5_KEYS // world
+    layers = CONFIG5_LAYERS
+    bytes_total = 2 * CONFIG5_KEYS * NKV * HD * 2  # K + V of the whole context, per layer
+
+    def timed(step) -> float:
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                step()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / steps / layers
+        if world > 1:
+            t = torch.tensor([us], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        del g
+        return us
+
+    # single-GPU reference: the whole context on rank 0 alone
+    t1 = None
+    if rank == 0:
+        kv1, q1, qpos1 = make_inputs(CONFIG5_KEYS, 0, 1, dev, seed=55, layers=layers)
+        out1 = torch.empty_like(q1)
+        ws1 = torch.empty(max(256, ops.decode_workspace_bytes(1, 1, NH, NKV, CONFIG5_KEYS)),
+                          dtype=torch.uint8, device=dev)
+
+        def step1():
+            for li in range(layers):
+                ops.gqa_decode(q1[li], kv1[li, 0], kv1[li, 1], qpos1, kv_layout="HND",
+                               out=out1[li], workspace=ws1, stable_prefix=True)
+
+        world_saved, world = world, 1  # time it without cross-rank barriers
+        t1 = timed(step1)
+        world = world_saved
+        del kv1
+        torch.cuda.empty_cache()
+    res = {"total_keys": CONFIG5_KEYS, "keys_per_rank": shard, "layers": layers,
+           "scaling": "strong (fixed context, 1/N of it per rank)",
+           "single_gpu_us_per_layer": None if t1 is None else round(t1, 2)}
+    if world == 1:
+        res["us_per_layer"] = round(t1, 2)
+        res["GBs"] = round(bytes_total / (t1 * 1e-6) / 1e9, 1)
+        return res
+    from solort_b200.sharded import ShardedDecode
+
+    kv, q, qpos = make_inputs(shard, rank, world, dev, seed=55, layers=layers)
+    outs = torch.empty_like(q)
+    ws = torch.empty(max(256, ops.decode_workspace_bytes(1, 1, NH, NKV, shard),
+                         ops.decode_exchange_workspace_bytes(1, 1, NH, NKV, shard)),
+                     dtype=torch.uint8, device=dev)
+    t1_all = torch.tensor([t1 or 0.0], dtype=torch.float64, device=dev)
+    dist.broadcast(t1_all, 0)
+    t1 = float(t1_all.item())
+    res["single_gpu_us_per_layer"] = round(t1, 2)
+    for exchange in ("p2p", "nccl"):
+        sd = ShardedDecode(rank, world, num_qo_heads=NH, layers=layers, device=dev,
+                           exchange=exchange)
+
+        def stepn():
+            for li in range(layers):
+                sd.layer(li, q[li], kv[li, 0], kv[li, 1], qpos, rank * shard, outs[li], ws,
+                         stable_prefix=True)
+
+        tn = timed(stepn)
+        sd.close()
+        res[exchange] = {"us_per_layer": round(tn, 2),
+                         "GBs_all_ranks": round(bytes_total / (tn * 1e-6) / 1e9, 1),
+                         "GBs_per_rank": round(bytes_total / world / (tn * 1e-6) / 1e9, 1),
+                         "strong_scaling_efficiency": round(t1 / (world * tn), 3)}
+    return res
+
+
 def run_gpu_arm(args) -> None:
     import torch
     import torch.distributed as dist
@@ -368,6 +476,8 @@ def run_gpu_arm(args) -> None:
     e2e_ms = timed_e2e(graph.replay)
     e2e_eager_ms = timed_e2e(eager_calls)
 
+    config5 = None if args.no_config5 else config5_bench(dev, rank, world, max(3, args.steps // 4))
+
     sweep = None
     if args.sweep and world == 1:
         sweep = _sweep(kv, q, qpos, ws, dev)
@@ -444,6 +554,8 @@ def run_gpu_arm(args) -> None:
                               "lse merge), NCCL all-gather kernels not counted"),
         "clocks": clk,
     }
+    if config5 is not None:
+        line["config5"] = config5
     if sweep:
         line["sweep"] = sweep
     if world == 1 and not args.no_extras:
