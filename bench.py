@@ -489,6 +489,7 @@ def run_gpu_arm(args) -> None:
     per_call_us = ms * 1e3 / LAYERS
     peaks = _peaks()
     achieved = bytes_per_layer / (per_call_us * 1e-6) / 1e9
+    traffic, traffic_src = _profiled_traffic("decode", ctx) if world == 1 else (None, None)
     line = {
         "metric": "GQA decode-attn HBM GB/s",
         "value": round(value, 1),
@@ -527,10 +528,10 @@ def run_gpu_arm(args) -> None:
             "peak_source": peaks[1],
             "algorithmic_bytes_per_launch": bytes_per_layer,
             "us_per_launch": round(per_call_us, 3),
-            "traffic": 33634560 if (world == 1 and ctx == 8192) else None,
-            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
-                              "decode_kernel launch of this workload "
-                              "(profiles/decode_splitkv_qwen3-4b_L8192_launches.md)",
+            "traffic": traffic,
+            "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                               f"decode_kernel launch of this workload ({traffic_src})"
+                               if traffic is not None else "no ncu capture of this shape"),
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
                 "h2d_bytes_per_step": q_host.numel() * 2,
@@ -789,9 +790,13 @@ def long_ctx_bench(dev, reps: int, ctx: int = 131072, layers: int = 36) -> dict:
     byt = 2 * ctx * NKV * HD * 2
     us = ms * 1e3 / layers
     del kv
+    traffic, traffic_src = _profiled_traffic("decode", ctx)
     return {"ctx": ctx, "layers": layers, "us_per_layer": round(us, 2),
             "GBs": round(byt / (us * 1e-6) / 1e9, 1),
-            "frac_of_measured_hbm": round(byt / (us * 1e-6) / 1e9 / _peaks()[0], 4)}
+            "frac_of_measured_hbm": round(byt / (us * 1e-6) / 1e9 / _peaks()[0], 4),
+            "kernel": "decode_tc_kernel (tcgen05, TMEM) + merge_kernel",
+            "algorithmic_bytes_per_launch": byt, "traffic": traffic,
+            "traffic_source": traffic_src}
 
 
 # Random-weight Qwen3 shapes for the end-to-end decode rate: (layers, hidden, intermediate,
@@ -920,6 +925,30 @@ def run_prefill_workload(args) -> None:
                        "T": int(T), "num_qo_heads": NH, "num_kv_heads": NKV, "head_dim": HD},
             "prefill": res}
     print(json.dumps(line), flush=True)
+
+
+# Committed ncu summaries that carry a per-launch DRAM traffic figure for a bench workload.
+TRAFFIC_PROFILES = {
+    ("decode", 8192): "profiles/decode_splitkv_qwen3-4b_L8192_launches.md",
+    ("decode", 131072): "profiles/decode_tc_qwen3-4b_L131072.md",
+}
+
+
+def _profiled_traffic(workload: str, keys: int):
+    """DRAM bytes (read + write) of one launch of the dominant kernel for this workload, read
+    from the `traffic_per_launch_bytes:` line of its committed ncu summary; (None, None) when no
+    capture covers the workload."""
+    rel = TRAFFIC_PROFILES.get((workload, keys))
+    if rel is None:
+        return None, None
+    try:
+        with open(os.path.join(ROOT, rel)) as fh:
+            for ln in fh:
+                if ln.startswith("traffic_per_launch_bytes:"):
+                    return int(ln.split(":", 1)[1].strip().replace(",", "")), rel
+    except OSError:
+        pass
+    return None, None
 
 
 def _peaks(tensor: bool = False):

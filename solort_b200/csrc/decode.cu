@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
 // lanes 0-15 hold keys 16w..16w+15, one column per query row. Four softmax warps read it, take
 // the tile's row maxima (16-lane shuffles, then the four warps through shared memory), keep one
 // running maximum per row with lazy rescaling (O in TMEM is rescaled only when a row's maximum
-// grows by more than 2^8), and write P^T as bf16 for the PV MMA. One thread issues the MMAs, one
+// grows by more than 2^64), and write P^T as bf16 for the PV MMA. One thread issues the MMAs, one
 // the TMA copies. 64-key tiles cycle through a 3-tile ring (three 8 KB slots in each of four 24 KB
 // regions: K dims 0-63, K dims 64-127, V dims 0-63, V dims 64-127); tiles past the ring are
 // prefetched into L2 so their refill is an L2 read. At the end each thread owns one head dim of
@@ -649,7 +649,8 @@ constexpr int kSoftmaxThreads = 128;
 constexpr uint32_t kTmemCols = 64;  // S^T x 2 (16 columns each), O^T (16)
 // Lazy rescaling: O^T in TMEM is rescaled only when a row's tile maximum exceeds the reference
 // it was accumulated against by more than 2^64 (log2 domain). P <= 2^64 stays finite in bf16, and
-// O and the row sums stay below 2^64 * 2^14 keys * |v| in fp32, far from overflow; scores of a real
+// O and the row sums stay below 2^64 * (keys in the split) * max|v| in fp32, far inside its 2^128
+// range for any split the plan makes (at most 2^31 keys) and |v| < 2^32; scores of a real
 // model rarely move the maximum that much, so the pipeline-draining rescale almost never runs.
 constexpr float kRescaleLog2 = 64.f;
 constexpr int kMinChunk = 2048;  // keys per split from which the plan picks this kernel
