@@ -489,7 +489,9 @@ def run_gpu_arm(args) -> None:
     per_call_us = ms * 1e3 / LAYERS
     peaks = _peaks()
     achieved = bytes_per_layer / (per_call_us * 1e-6) / 1e9
-    traffic, traffic_src = _profiled_traffic("decode", ctx) if world == 1 else (None, None)
+    # Each rank's decode launch is the single-GPU launch of its ctx keys (the exchange changes only
+    # where the merge sends the rows), so the same capture gives its traffic.
+    traffic, traffic_src = _profiled_traffic("decode", ctx)
     line = {
         "metric": "GQA decode-attn HBM GB/s",
         "value": round(value, 1),
@@ -530,7 +532,8 @@ def run_gpu_arm(args) -> None:
             "us_per_launch": round(per_call_us, 3),
             "traffic": traffic,
             "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
-                               f"decode_kernel launch of this workload ({traffic_src})"
+                               f"decode_kernel launch of this workload"
+                               + (" (per rank)" if world > 1 else "") + f" ({traffic_src})"
                                if traffic is not None else "no ncu capture of this shape"),
         },
         "e2e": {"value": round(e2e_value, 1), "unit": "GB/s",
