@@ -39,3 +39,20 @@ def test_header_constants_match_the_binding():
     assert int(re.search(r"#define SOLORT_MAX_RANKS (\d+)", text).group(1)) == _lib.MAX_RANKS
     abi = int(re.search(r"#define SOLORT_ATTN_ABI_VERSION (\d+)", text).group(1))
     assert _lib.load().solort_attn_abi_version() == abi
+
+
+def test_roofline_traffic_comes_from_committed_ncu_summaries():
+    """Every workload with a committed ncu capture yields its per-launch DRAM bytes from the
+    summary's `traffic_per_launch_bytes:` line, and the figure is close to the algorithmic bytes
+    of one launch (K + V read once: 4096 bytes per key for 32/8 heads at head_dim 128)."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    assert bench.TRAFFIC_PROFILES
+    for (workload, keys), rel in bench.TRAFFIC_PROFILES.items():
+        assert os.path.exists(os.path.join(ROOT, rel)), rel
+        traffic, src = bench._profiled_traffic(workload, keys)
+        assert src == rel and isinstance(traffic, int)
+        algorithmic = 4096 * keys
+        assert algorithmic <= traffic <= 1.05 * algorithmic, (rel, traffic, algorithmic)
+    assert bench._profiled_traffic("decode", 12345) == (None, None)
