@@ -714,7 +714,6 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
   const int rows_total = p.batch * p.q_len * p.nh;
   const bool single = p.num_splits == 1 && !p.force_partial;
 
-  pdl_launch_dependents();
   if (sbase & 1023u) {
     if (tid == 0) atomicOr(&g_decode_status, kDevErrSmemAlign);
     return;
@@ -782,6 +781,9 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
   umma::fence_before();
   __syncthreads();
   umma::fence_after();
+  // The next kernel may launch once every CTA holds its TMEM (a dependent CTA that took the
+  // columns first would wait on this grid while this CTA waited on the columns).
+  pdl_launch_dependents();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tO = tmem + 2 * kN;
 

@@ -276,6 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Launched as a programmatic dependent: everything above (barriers, TMEM) overlaps the previous
+  // kernel's tail; Q, K, V and the output are touched only after it has finished. The next kernel
+  // may launch only now, once every CTA holds its TMEM: a dependent CTA that took the columns
+  // first would wait on this grid while this CTA waited on the columns.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS[2] = {tmem, tmem + kBN};
   const uint32_t tO = tmem + 2 * kBN;
@@ -629,6 +635,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // Launched as a programmatic dependent: everything above (barriers, TMEM) overlaps the previous
+  // kernel's tail; Q, K, V and the output are touched only after it has finished. The next kernel
+  // may launch only now, once every CTA holds its TMEM: a dependent CTA that took the columns
+  // first would wait on this grid while this CTA waited on the columns.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS[2] = {tmem, tmem + 2 * kBN};
   const uint32_t tO[2] = {tmem + kBN, tmem + 3 * kBN};
@@ -967,11 +979,18 @@ extern "C" int solort_attn_prefill(const SolortPrefillArgs* a, void* stream_v) {
       return SOLORT_ERR_CUDA;
     if (dev < 32) configured.fetch_or(1u << dev, std::memory_order_release);
   }
-  if (ping_pong)
-    pp::prefill_pp_kernel<<<static_cast<unsigned>(grid), kThreads, pp::kSmemBytes,
-                            static_cast<cudaStream_t>(stream_v)>>>(tq, tk, tv, prm);
-  else
-    prefill_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes,
-                     static_cast<cudaStream_t>(stream_v)>>>(tq, tk, tv, prm);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = ping_pong ? pp::kSmemBytes : kSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(stream_v);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = ping_pong ? cudaLaunchKernelEx(&cfg, pp::prefill_pp_kernel, tq, tk, tv, prm)
+                                  : cudaLaunchKernelEx(&cfg, prefill_kernel, tq, tk, tv, prm);
+  if (e != cudaSuccess) return SOLORT_ERR_CUDA;
   return launch_status();
 }
