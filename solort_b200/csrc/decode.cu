@@ -62,7 +62,8 @@ struct Shape {
   static constexpr int kThreads = kProducerWarp ? 160 : 128;
 };
 constexpr int kMaxPagedChunk = 16384;       // tokens per split at most with a block table
-constexpr int kMinSplitTiles = 4;           // default plans: at least 128 keys per split
+constexpr int kMinSplitTiles = 2;           // default plans: at least 64 keys per split
+constexpr int kSingleSplitKeys = 128;       // default plans: one split up to this many keys
 constexpr int kMergeWarps = 8;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -1296,10 +1297,15 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl, bool force_partial = false) {
   // Two CTAs per SM are resident; size the splits so the grid is one such wave.
   const int64_t resident = 2ll * di.sm_count;
   const int64_t heads = static_cast<int64_t>(a->batch) * a->num_kv_heads;
-  // One resident wave of splits, but at least kMinSplitTiles tiles per split: a split of one or
-  // two tiles is all fixed cost (set-up, combine, partial store) and adds a partial to the merge.
+  // One resident wave of splits, but at least kMinSplitTiles tiles per split (a one-tile split is
+  // all fixed cost and one more partial for the merge), and a single split, with no merge, up to
+  // kSingleSplitKeys keys. Measured per call (32/8 heads, stable prefix): 64-key splits against
+  // 128-key ones take L = 1024 from 6.76 to 5.98 us and L = 512 from 6.20 to 5.98; at L = 128 two
+  // splits and a merge take 5.2 us against 3.6 for one split.
   const int64_t wave = resident / heads > 1 ? resident / heads : 1;
-  const int64_t by_len = ceil_div(pl->kv_limit, static_cast<int64_t>(kMinSplitTiles) * kTile);
+  const int64_t by_len = pl->kv_limit <= kSingleSplitKeys
+                             ? 1
+                             : ceil_div(pl->kv_limit, static_cast<int64_t>(kMinSplitTiles) * kTile);
   const int64_t target = a->num_splits > 0 ? a->num_splits : (by_len < wave ? by_len : wave);
   int64_t chunk = ceil_div(ceil_div(pl->kv_limit, target), kBox) * kBox;
   if (pl->paged && chunk > kMaxPagedChunk) chunk = kMaxPagedChunk;
