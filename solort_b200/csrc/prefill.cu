@@ -46,6 +46,7 @@ constexpr int kSoftmaxThreads = 256;         // two warp groups
 constexpr int kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.f;          // lazy rescale threshold (factor 256)
 constexpr int kPingPongMinTiles = 16;        // 128-row query tiles from which two go per CTA
+constexpr int kStageRow = kHD * 2 + 16;      // bytes per row of the output tile staged for the store
 
 // shared memory map (offsets from a 1024-aligned base)
 constexpr int kOffQ = 0;
@@ -77,7 +78,8 @@ enum {
   kBarPVDone = kBarPFull + 1,        // PV_j committed
   kBarXMax = kBarPVDone + 1,         // +parity*4 + warp pair (8), 64 arrivals: row-max exchange
   kBarXSum = kBarXMax + 8,           // 256 arrivals: final row-sum exchange
-  kNumBars = kBarXSum + 1
+  kBarOStaged = kBarXSum + 1,        // 256 arrivals: the output tile staged in shared memory
+  kNumBars = kBarOStaged + 1
 };
 
 __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
@@ -258,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < kNumBars; ++i) {
       const uint32_t count =
-          (i == kBarPFull || i == kBarXSum) ? kSoftmaxThreads
+          (i == kBarPFull || i == kBarXSum || i == kBarOStaged) ? kSoftmaxThreads
           : (i >= kBarXMax && i < kBarXMax + 8) ? 64u
                                                  : 1u;
       mbar_init(&bars[i], count);
@@ -478,24 +480,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (__all_sync(0xffffffffu, wait_bar(&bars[kBarXSum], 0, abort_flag))) {
         const float total = l_sum + xsum[(g ^ 1) * kBM + r];
         const float inv = total > 0.f ? 1.f / total : 0.f;
-        const bool write = qi < p.q_len;
-        bf16* orow = p.out + static_cast<int64_t>(qi) * p.o_st +
-                     static_cast<int64_t>(head) * p.o_sh + 64 * g;
+        // The normalised tile goes through shared memory (the K ring, idle once every MMA is done;
+        // rows padded to kStageRow bytes so a warp's 32 rows fall in distinct bank groups), then
+        // out in whole rows: a thread's own row is 8 KB from its neighbour's, so direct stores
+        // would touch 32 half sectors per instruction (1.2 us of the epilogue).
+        uint8_t* stage = smem + kOffK;
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           float v[32];
           tmem_ld32(tO + lane_off + 64 * g + c * 32, v);
           tmem_wait_ld();
-          if (write) {
 #pragma unroll
-            for (int q8 = 0; q8 < 4; ++q8) {
-              uint4 o4;
-              o4.x = pack_bf16x2(v[q8 * 8 + 0] * inv, v[q8 * 8 + 1] * inv);
-              o4.y = pack_bf16x2(v[q8 * 8 + 2] * inv, v[q8 * 8 + 3] * inv);
-              o4.z = pack_bf16x2(v[q8 * 8 + 4] * inv, v[q8 * 8 + 5] * inv);
-              o4.w = pack_bf16x2(v[q8 * 8 + 6] * inv, v[q8 * 8 + 7] * inv);
-              *reinterpret_cast<uint4*>(orow + c * 32 + q8 * 8) = o4;
-            }
+          for (int q8 = 0; q8 < 4; ++q8) {
+            uint4 o4;
+            o4.x = pack_bf16x2(v[q8 * 8 + 0] * inv, v[q8 * 8 + 1] * inv);
+            o4.y = pack_bf16x2(v[q8 * 8 + 2] * inv, v[q8 * 8 + 3] * inv);
+            o4.z = pack_bf16x2(v[q8 * 8 + 4] * inv, v[q8 * 8 + 5] * inv);
+            o4.w = pack_bf16x2(v[q8 * 8 + 6] * inv, v[q8 * 8 + 7] * inv);
+            *reinterpret_cast<uint4*>(stage + r * kStageRow + g * 128 + c * 64 + q8 * 16) = o4;
+          }
+        }
+        mbar_arrive(&bars[kBarOStaged]);
+        if (__all_sync(0xffffffffu, wait_bar(&bars[kBarOStaged], 0, abort_flag))) {
+          for (int i = tid - 128; i < kBM * 16; i += kSoftmaxThreads) {
+            const int row = i >> 4, ch = i & 15;
+            if (q0 + row < p.q_len)
+              *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(q0 + row) * p.o_st +
+                                        static_cast<int64_t>(head) * p.o_sh + ch * 8) =
+                  *reinterpret_cast<const uint4*>(stage + row * kStageRow + ch * 16);
           }
         }
       }
