@@ -53,6 +53,12 @@ constexpr int kMaxStages = 7;               // 112 KB: a 224-key split is reques
 // it reaches last, and holding it back leaves 4.6 MB less queued in front of the previous call's
 // merge and release. L = 8192, 36-layer graph: 10.16 -> 9.98 us per call (2-4 early: 10.6-10.9).
 constexpr int kEarlyStages = 5;
+// HOLD instances (splits of 5 to 7 tiles that fit the ring, stable prefix): only kHoldEarlyStages
+// go out before the wait, and the other stable tiles with the last stage once the query rows are
+// staged. L = 8192, 36-layer graph, per call: 9.90 -> 9.56 us. Kept a separate instance because
+// the same code in the instance the runner's two-tile splits use (where it issues exactly the same
+// tiles) cost that step ~1 us per decode call.
+constexpr int kHoldEarlyStages = 4;
 // Two CTAs per SM: 228 KB of shared memory per SM, less 1 KB the hardware keeps per CTA.
 constexpr int kSmemPerCta = 115712;
 // After the ring: full barriers, flags, the tile last issued into each stage, block-table slice.
@@ -126,7 +132,7 @@ __device__ __forceinline__ void write_partial(const Params& p, int split, int ro
   if (c == 0) p.part_lse[static_cast<int64_t>(split) * rows_total + R] = lse;
 }
 
-template <int MT, bool PAGED>
+template <int MT, bool PAGED, bool HOLD>
 __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
     decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                   const Params p) {
@@ -262,18 +268,25 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
 
   // Every stage but the last is filled at once; the last one first carries this CTA's query rows.
   // Tiles whose keys all lie below q_pos go out before the wait when the prefix is stable.
+  int defer_i = 0, defer_n = 0;  // HOLD: stable tiles held back until the query rows are staged
   if (initial_issuer) {
     const int n0 = ntiles < nst - 1 ? ntiles : nst - 1;
     int i = 0;
     if (early) {
       const long long stable_end = qpos - p.kv_pos_offset;  // local keys below it are stable
-      while (i < n0 && i < kEarlyStages && min(t_begin + (i + 1) * kTile, t_end) <= stable_end) {
+      const int n_early = HOLD ? kHoldEarlyStages : kEarlyStages;
+      while (i < n0 && i < n_early && min(t_begin + (i + 1) * kTile, t_end) <= stable_end) {
         issue(i, i);
         ++i;
       }
+      if (HOLD) {
+        defer_i = i;
+        while (i < n0 && min(t_begin + (i + 1) * kTile, t_end) <= stable_end) ++i;
+        defer_n = i;
+      }
     }
     if (early) pdl_wait();
-    for (; i < n0; ++i) issue(i, i);
+    for (; i < n0; ++i) issue(i, i);  // HOLD: the tiles holding q_pos and later keys
   } else if (early) {
     pdl_wait();
   }
@@ -323,7 +336,17 @@ __global__ void __launch_bounds__(Shape<MT>::kThreads, 2)
     __syncwarp();
     asm volatile("bar.sync 4, %0;" ::"n"((kWarps + 1) * 32) : "memory");
   }
-  if (initial_issuer && ntiles >= nst) issue(nst - 1, nst - 1);
+  if (HOLD) {
+    // The held-back tiles and the last stage from one issue site (each inlined copy of `issue` is a
+    // few hundred bytes of the kernel's code).
+    if (initial_issuer) {
+      const int last = ntiles >= nst ? nst - 1 : -1;
+      for (int t = defer_i; t < nst; ++t)
+        if (t < defer_n || t == last) issue(t, t);
+    }
+  } else if (initial_issuer && ntiles >= nst) {
+    issue(nst - 1, nst - 1);
+  }
 
   int lim[MT][2];  // last visible local key of the two rows this lane holds per m-tile
 #pragma unroll
@@ -1264,6 +1287,7 @@ struct Plan {
   int splits = 0;
   int stages = kMaxStages;
   bool force_partial = false;  // exchange calls always merge through the partials
+  bool hold = false;           // decode_kernel holds stable tiles back (see kHoldEarlyStages)
   size_t part_o_bytes = 0;
   size_t part_lse_bytes = 0;
   size_t ws_bytes = 0;
@@ -1340,6 +1364,8 @@ int make_plan(const SolortDecodeArgs* a, Plan* pl, bool force_partial = false) {
   pl->stages = bt_ints * 4 <= spare ? kMaxStages : kMaxStages - 1;
   pl->smem_bytes = static_cast<size_t>(pl->stages) * kStageBytes + kHdrBytes + bt_ints * 4;
   if (pl->smem_bytes > static_cast<size_t>(kSmemPerCta)) return SOLORT_ERR_UNSUPPORTED;
+  pl->hold = pl->mt == 1 && (a->flags & SOLORT_DECODE_STABLE_PREFIX) &&
+             pl->chunk > kHoldEarlyStages * kTile && pl->chunk <= pl->stages * kTile;
   return SOLORT_OK;
 }
 
@@ -1357,7 +1383,7 @@ inline cudaLaunchConfig_t pdl_config(dim3 grid, dim3 block, size_t smem, cudaStr
   return cfg;
 }
 
-template <int MT, bool PAGED>
+template <int MT, bool PAGED, bool HOLD = false>
 int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& prm, dim3 grid,
                   size_t smem, cudaStream_t stream) {
   static std::atomic<unsigned> configured{0};  // one bit per device ordinal < 32
@@ -1366,9 +1392,9 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& pr
   const size_t max_smem = kSmemPerCta;
   if (smem > max_smem) return SOLORT_ERR_UNSUPPORTED;
   if (dev >= 32 || !(configured.load(std::memory_order_acquire) & (1u << dev))) {
-    if (cudaFuncSetAttribute(decode_kernel<MT, PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(decode_kernel<MT, PAGED, HOLD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(max_smem)) != cudaSuccess ||
-        cudaFuncSetAttribute(decode_kernel<MT, PAGED>,
+        cudaFuncSetAttribute(decode_kernel<MT, PAGED, HOLD>,
                              cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
       return SOLORT_ERR_CUDA;
@@ -1376,7 +1402,7 @@ int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const Params& pr
   }
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(grid, dim3(Shape<MT>::kThreads), smem, stream, attr);
-  if (cudaLaunchKernelEx(&cfg, decode_kernel<MT, PAGED>, tk, tv, prm) != cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, decode_kernel<MT, PAGED, HOLD>, tk, tv, prm) != cudaSuccess)
     return SOLORT_ERR_CUDA;
   return launch_status();
 }
@@ -1611,8 +1637,12 @@ int decode_impl(const SolortDecodeArgs* a, const SolortExchangeArgs* x, void* st
     rc = pl.paged ? launch_decode_tc<true, 4>(tk, tv, prm, grid, pl.smem_bytes, stream)
                   : launch_decode_tc<false, 4>(tk, tv, prm, grid, pl.smem_bytes, stream);
   } else if (pl.mt == 1) {
-    rc = pl.paged ? launch_decode<1, true>(tk, tv, prm, grid, pl.smem_bytes, stream)
-                  : launch_decode<1, false>(tk, tv, prm, grid, pl.smem_bytes, stream);
+    if (pl.hold)
+      rc = pl.paged ? launch_decode<1, true, true>(tk, tv, prm, grid, pl.smem_bytes, stream)
+                    : launch_decode<1, false, true>(tk, tv, prm, grid, pl.smem_bytes, stream);
+    else
+      rc = pl.paged ? launch_decode<1, true>(tk, tv, prm, grid, pl.smem_bytes, stream)
+                    : launch_decode<1, false>(tk, tv, prm, grid, pl.smem_bytes, stream);
   } else {
     rc = pl.paged ? launch_decode<2, true>(tk, tv, prm, grid, pl.smem_bytes, stream)
                   : launch_decode<2, false>(tk, tv, prm, grid, pl.smem_bytes, stream);
