@@ -688,7 +688,9 @@ def prefill_bench(dev, steps: int, warmup: int, lengths=(512, 1024, 4096)) -> di
         del graph, sets
     res["peak_tflops"] = peak
     res["peak_source"] = src
-    res["kernel"] = "prefill_kernel (tcgen05.mma M128 N128, TMEM accumulators, TMA-fed)"
+    res["kernel"] = ("tcgen05.mma M128 N128, TMEM accumulators, TMA-fed: prefill_kernel (one CTA per "
+                     "query tile and head), prefill_items_kernel (persistent, when those items "
+                     "outnumber the SMs), prefill_pp_kernel (two query tiles per CTA, >= 16 tiles)")
     return res
 
 

@@ -49,6 +49,25 @@ def test_prefill_bottom_right_over_cache(q_len, kv_len):
     _close(out, lit, "vs the bridge's torch fallback")
 
 
+@pytest.mark.parametrize("q_len,kv_len,nh,causal",
+                         [(1900, 1900, 32, True), (1900, 1900, 16, True), (1500, 1800, 32, True),
+                          (1000, 2000, 32, False)])
+def test_prefill_persistent_items(q_len, kv_len, nh, causal):
+    """More (query tile, head) items than SMs: each persistent CTA of the one-tile kernel walks
+    several items (up to four at q_len 1900 with 32 heads on 148 SMs), with the Q and O buffers
+    alternating between items and each output tile stored after the next item's first tile."""
+    from solort_b200 import ops
+
+    off = kv_len - q_len if causal else 10 ** 6
+    q, k, v = A.make_attention_inputs(11 + q_len + nh, nh, 8, 128, q_len, kv_len,
+                                      kv_len - q_len)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, off)
+    out = ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda(), causal=causal)
+    torch.cuda.synchronize()
+    _close(out, ref, f"persistent q={q_len} kv={kv_len} nh={nh} causal={causal}")
+    assert ops.device_status() == 0
+
+
 def test_prefill_non_causal():
     from solort_b200 import ops
 
