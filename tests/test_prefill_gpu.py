@@ -68,6 +68,24 @@ def test_prefill_persistent_items(q_len, kv_len, nh, causal):
     assert ops.device_status() == 0
 
 
+def test_prefill_persistent_head_major_views():
+    """The persistent kernel over head-major storage ([heads, T, hd] tensors viewed as [T, heads,
+    hd]): the tensor maps then take (dim, token, head) coordinates instead of (dim, head, token)."""
+    from solort_b200 import ops
+
+    T, nh, nkv = 1100, 32, 8  # 9 query tiles x 32 heads = 288 items on at most 148 CTAs
+    q, k, v = A.make_attention_inputs(21, nh, nkv, 128, T, T, 0)
+    qh = q.transpose(0, 1).contiguous().cuda().transpose(0, 1)
+    kh = k.transpose(0, 1).contiguous().cuda().transpose(0, 1)
+    vh = v.transpose(0, 1).contiguous().cuda().transpose(0, 1)
+    assert qh.stride(1) > qh.stride(0)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, 0)
+    out = ops.gqa_prefill(qh, kh, vh)
+    torch.cuda.synchronize()
+    _close(out, ref, "persistent, head-major views")
+    assert ops.device_status() == 0
+
+
 def test_prefill_non_causal():
     from solort_b200 import ops
 
