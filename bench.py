@@ -43,6 +43,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--ctx", type=int, default=8192, help="keys per GPU")
+    ap.add_argument("--long-ctx", type=int, default=131072,
+                    help="--workload long: keys per layer (131072 = BASELINE config 5; a "
+                    "1/N shard of it times one rank's local decode without the exchange)")
     ap.add_argument("--cpu-sample-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sweep", action="store_true", help="also time L in {128..8192}")
@@ -799,7 +802,8 @@ def long_ctx_bench(dev, reps: int, ctx: int = 131072, layers: int = 36) -> dict:
     return {"ctx": ctx, "layers": layers, "us_per_layer": round(us, 2),
             "GBs": round(byt / (us * 1e-6) / 1e9, 1),
             "frac_of_measured_hbm": round(byt / (us * 1e-6) / 1e9 / _peaks()[0], 4),
-            "kernel": "decode_tc_kernel (tcgen05, TMEM) + merge_kernel",
+            "kernel": "decode_tc_kernel (tcgen05, TMEM; splits of >= 2048 keys) or decode_kernel, "
+                      "+ merge_kernel",
             "algorithmic_bytes_per_launch": byt, "traffic": traffic,
             "traffic_source": traffic_src}
 
@@ -903,14 +907,15 @@ def run_long_workload(args) -> None:
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
-    res = long_ctx_bench(dev, max(3, args.steps), layers=args.layers)
+    res = long_ctx_bench(dev, max(3, args.steps), ctx=args.long_ctx, layers=args.layers)
     line = {"metric": "long-context decode-attn HBM GB/s", "value": res["GBs"], "unit": "GB/s",
             "n_gpus": 1, "steps": max(3, args.steps), "warmup": 3,
             "ms_per_step": round(res["us_per_layer"] * args.layers / 1e3, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": "qwen3-4b decode over 131072 keys (BASELINE config 5, 1 GPU)",
-                       "layers": args.layers},
+            "config": {"workload": f"qwen3-4b decode over {args.long_ctx} keys (BASELINE config 5"
+                                   f"{'' if args.long_ctx == 131072 else ', one shard of it'}, 1 GPU)",
+                       "keys": args.long_ctx, "layers": args.layers},
             "peak_source": _peaks()[1], "long_ctx": res}
     print(json.dumps(line), flush=True)
 
