@@ -569,7 +569,8 @@ constexpr int kSmemBytes = 1024 + kOffBar + 512;
 // the CTA's running count of K/V tiles over all its items.
 enum {
   kBarQFull = 0,                     // +item parity: Q tile landed
-  kBarQEmpty = kBarQFull + 2,        // +item parity, 256 arrivals: output stored, buffer free
+  kBarQEmpty = kBarQFull + 2,        // +item parity, 256 arrivals: the staged output read back,
+                                     // buffer free (arrived only if item k + 2 exists)
   kBarKFull = kBarQEmpty + 2,        // +stage
   kBarKEmpty = kBarKFull + kStages,
   kBarVFull = kBarKEmpty + kStages,
@@ -584,10 +585,10 @@ enum {
   kNumBars = kBarOStaged + 1
 };
 
-// Work items: (128-row query tile, query head) pairs, heaviest query
-// tiles first (item w = query tile q_tiles - 1 - w / nh of head w % nh). CTA c of a grid of G
-// takes items c, 2G - 1 - c, 2G + c, 4G - 1 - c, ...: a snake over the grid that gives the CTAs
-// holding the heaviest first items the lightest second ones.
+// Work items: (128-row query tile, query head) pairs, heaviest query tiles first (item w = query
+// tile q_tiles - 1 - w / nh of head w % nh). CTA c of a grid of G takes items c, 2G - 1 - c,
+// 2G + c, 4G - 1 - c, ...: a snake over the grid that gives the CTAs holding the heaviest first
+// items the lightest second ones.
 __device__ __forceinline__ int item_of(int k, int c, int grid) {
   return k * grid + ((k & 1) ? grid - 1 - c : c);
 }
