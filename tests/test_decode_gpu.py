@@ -67,6 +67,40 @@ def test_decode_full_size_config5_one_gpu():
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("nh,nkv,q_len,L,splits", [
+    (8, 8, 1, 3000, None),     # group 1 (one query head per KV head)
+    (8, 8, 4, 5000, None),     # group 1, four verify rows
+    (8, 8, 1, 8192, 2),        # group 1, 4096-key splits: the tcgen05 decode kernel
+    (16, 16, 2, 8192, 2),      # group 1, two rows on the tcgen05 kernel
+    (64, 8, 1, 4097, None),    # group 8
+    (64, 8, 4, 3000, None),    # group 8 x 4 tokens = 32 rows per KV head, the limit
+    (32, 2, 2, 2500, None),    # group 16 x 2 tokens = 32 rows
+    (32, 1, 1, 1500, None),    # group 32: a single KV head
+])
+def test_decode_other_group_sizes(nh, nkv, q_len, L, splits):
+    """GQA groups other than Qwen3's 4 and 2, up to the 32 query rows a KV head's CTA packs into
+    its tensor-core tiles, on both decode kernels."""
+    ops = _ops()
+    q, k, v = _static_case(nh * 131 + q_len + L, nh, nkv, L, q_len)
+    ref, _ = A.attention_fp32(q, k, v, 128**-0.5, L - q_len)
+    qpos = torch.tensor([L - q_len], dtype=torch.int64, device="cuda")
+    kw = {} if splits is None else {"num_splits": splits}
+    out = ops.gqa_decode(q[None].cuda(), k.cuda(), v.cuda(), qpos, **kw)
+    torch.cuda.synchronize()
+    assert_close(out[0], ref, f"nh={nh} nkv={nkv} q_len={q_len} L={L} splits={splits}")
+    assert ops.device_status() == 0
+
+
+def test_decode_rejects_more_than_32_rows_per_kv_head():
+    ops = _ops()
+    q, k, v = _static_case(3, 64, 8, 600, 5)  # group 8 x 5 tokens = 40 rows
+    qpos = torch.tensor([595], dtype=torch.int64, device="cuda")
+    with pytest.raises(RuntimeError):
+        ops.gqa_decode(q[None].cuda(), k.cuda(), v.cuda(), qpos)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("splits", [1, 2, 3, 17])
 def test_decode_forced_splits(splits):
     ops = _ops()

@@ -86,6 +86,27 @@ def test_prefill_persistent_head_major_views():
     assert ops.device_status() == 0
 
 
+@pytest.mark.parametrize("nh,nkv,T", [
+    (64, 8, 700),      # group 8, one CTA per (query tile, head)
+    (48, 16, 1100),    # group 3, persistent kernel (9 tiles x 48 heads = 432 items)
+    (32, 2, 1500),     # group 16, persistent kernel
+    (12, 12, 900),     # group 1 (multi-head), 12 heads
+    (40, 8, 2300),     # group 5, two-tile kernel (9 pairs x 40 heads = 360 CTAs)
+    (8, 1, 2100),      # group 8 over a single KV head, two-tile kernel with an odd tile count
+])
+def test_prefill_other_group_sizes(nh, nkv, T):
+    """GQA groups other than Qwen3's, across the three prefill kernels: query head h reads KV head
+    h / (nh / nkv) through the tensor maps, with no K/V expansion."""
+    from solort_b200 import ops
+
+    q, k, v = A.make_attention_inputs(T + 17 * nh + nkv, nh, nkv, 128, T, T, 0)
+    ref, _ = A.attention_fp32(q, k, v, 128 ** -0.5, 0)
+    out = ops.gqa_prefill(q.cuda(), k.cuda(), v.cuda())
+    torch.cuda.synchronize()
+    _close(out, ref, f"prefill nh={nh} nkv={nkv} T={T}")
+    assert ops.device_status() == 0
+
+
 def test_prefill_non_causal():
     from solort_b200 import ops
 
