@@ -55,7 +55,8 @@ constexpr int kMaxStages = 7;               // 112 KB: a 224-key split is reques
 constexpr int kEarlyStages = 5;
 // HOLD instances (splits of 5 to 7 tiles that fit the ring, stable prefix): only kHoldEarlyStages
 // go out before the wait, and the other stable tiles with the last stage once the query rows are
-// staged. L = 8192, 36-layer graph, per call: 9.90 -> 9.56 us. Kept a separate instance because
+// staged. L = 8192, 36-layer graph, per call: 9.90 -> 9.56 us (3 / 5 / 6 stages early: 9.93 /
+// 9.82 / 10.17 against 9.63 for 4 in one A/B run). Kept a separate instance because
 // the same code in the instance the runner's two-tile splits use (where it issues exactly the same
 // tiles) cost that step ~1 us per decode call.
 constexpr int kHoldEarlyStages = 4;
