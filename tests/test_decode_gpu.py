@@ -365,6 +365,29 @@ def test_paged_page_sizes(P):
     assert_close(out[0], ref, f"paged P={P}")
 
 
+@pytest.mark.parametrize("nh,nkv,q_len,P,n,splits", [
+    (32, 8, 1, 256, 3000, None),    # pages larger than one TMA box of rows
+    (32, 8, 4, 1024, 5000, None),   # verify over 1024-token pages
+    (8, 8, 4, 16, 2000, None),      # group 1, four verify rows
+    (64, 8, 4, 16, 2000, None),     # group 8 x 4 tokens = 32 rows per KV head
+    (8, 8, 1, 16, 8192, 2),         # group 1, 4096-key splits: the tcgen05 kernel, paged
+])
+def test_paged_groups_and_large_pages(nh, nkv, q_len, P, n, splits):
+    """Paged decode / verify beyond Qwen3's shape: other GQA groups, the tcgen05 kernel reading
+    pages, and pages of 256 and 1024 tokens, from a seeded-permutation block table."""
+    ops = _ops()
+    q, k, v = A.make_attention_inputs(n + P + nh, nh, nkv, 128, q_len, n, n - q_len)
+    arena, tables = _paged_setup(P + nh, [(n, k, v)], P, OP.pages_required(n, P) + 3, nkv=nkv)
+    ref, _ = A.attention_fp32(q, k, v, 128**-0.5, n - q_len)
+    bt = torch.tensor([tables[0]], dtype=torch.int32).cuda()
+    qpos = torch.tensor([n - q_len], dtype=torch.int64, device="cuda")
+    kw = {} if splits is None else {"num_splits": splits}
+    out = ops.gqa_decode_paged(q[None].cuda(), arena.cuda(), bt, qpos, max_kv_len=n, **kw)
+    torch.cuda.synchronize()
+    assert_close(out[0], ref, f"paged nh={nh} nkv={nkv} q_len={q_len} P={P} splits={splits}")
+    assert ops.device_status() == 0
+
+
 @pytest.mark.parametrize("R", [2, 4, 8])
 def test_sharded_partials_merge(R):
     """Sequence-sharded decode on one GPU: R shards -> partial (O, LSE) -> lse_merge."""
